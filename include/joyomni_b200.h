@@ -1,0 +1,119 @@
+/*
+ * joyomni_b200 — C ABI of the B200-native (sm_100a) joyomni_ops operator set.
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t passed
+ * as `void*` (NULL = legacy default stream), enqueues its kernels on that
+ * stream, never synchronises the host and never allocates device memory, so
+ * every call can be captured in a CUDA graph.  Each returns JO_OK (0) or a
+ * negative JO_ERR_* status; the message is in jo_last_error() (thread-local).
+ *
+ * Reference interfaces replaced (paths inside jd-opensource/JoyAI-Video-Edit):
+ *   deploy/joyomni_ops/csrc/pybind.cpp:33-58          TORCH_LIBRARY(joyomni_ops) schema
+ *   deploy/joyomni_ops/joyomni_ops/__init__.py:31-58  Python wrappers
+ */
+#ifndef JOYOMNI_B200_H_
+#define JOYOMNI_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define JO_OK 0
+#define JO_ERR_INVALID (-1)   /* bad shape / size / argument  -> RuntimeError        */
+#define JO_ERR_DTYPE (-2)     /* unsupported dtype            -> RuntimeError        */
+#define JO_ERR_ALIGN (-3)     /* misaligned pointer / stride  -> RuntimeError        */
+#define JO_ERR_ARCH (-4)      /* device is not sm_100         -> NotImplementedError */
+#define JO_ERR_CUDA (-5)      /* CUDA runtime / launch error  -> RuntimeError        */
+
+/* ---- dtype tags ------------------------------------------------------ */
+#define JO_DTYPE_F32 0
+#define JO_DTYPE_F16 1
+#define JO_DTYPE_BF16 2
+#define JO_DTYPE_E4M3 3
+
+/* ---- norm types (deploy/joyomni_ops/csrc/fused_norm_scale_shift.cu:25) - */
+#define JO_NORM_LAYER 0
+#define JO_NORM_RMS 1
+
+/* ---- GEMM epilogues --------------------------------------------------- */
+#define JO_EPI_NONE 0
+#define JO_EPI_GELU_TANH 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+int jo_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* jo_last_error(void);
+
+/* Compute capability (major*10+minor) of `device`, or a negative status. */
+int jo_device_arch(int device);
+
+/*
+ * Fused per-head RMSNorm + interleaved-pair 3D RoPE, in place on q and k.
+ * Replaces joyomni_ops::fused_qk_norm_rope_3d_paired
+ *   (deploy/joyomni_ops/csrc/fused_qknorm_rope_3d_kernel.cu:179-208).
+ * q, k: bf16 [batch, seq_len*num_heads, head_dim], contiguous, 16-byte aligned.
+ * q_weight, k_weight: bf16 [head_dim].  cos, sin: bf16 [seq_len, head_dim/2].
+ * head_dim in {64, 128, 256}.
+ */
+int jo_fused_qk_norm_rope_3d_paired(void* q, void* k, int64_t batch, int64_t seq_len,
+                                    int64_t num_heads, int64_t head_dim, float eps,
+                                    const void* q_weight, const void* k_weight,
+                                    const void* cos, const void* sin, void* stream);
+
+/*
+ * y = Norm(x; gamma, beta) * (1 + scale) + shift, norm_type JO_NORM_LAYER/RMS.
+ * Replaces joyomni_ops::fused_norm_scale_shift
+ *   (deploy/joyomni_ops/csrc/fused_norm_scale_shift.cu:172-209).
+ * x: [M, N] with row stride x_stride (elements); y: [M, N] dense.
+ * gamma, beta: NULL or [N] of x's dtype (beta used only by LayerNorm, and only
+ * when gamma is given, as in the reference).  scale, shift: rows of N elements
+ * with row stride mod_stride; x-row m reads modulation row m / mod_group
+ * (mod_group = 1 is the reference's per-row [M, N] layout; mod_group = L
+ * broadcasts a [B, N] table over L tokens; mod_stride = 0 broadcasts one [N]
+ * vector).  N % 4 == 0.  dtype: JO_DTYPE_F32/F16/BF16.
+ */
+int jo_fused_norm_scale_shift(void* y, const void* x, const void* gamma, const void* beta,
+                              const void* scale, const void* shift, int64_t M, int64_t N,
+                              int64_t x_stride, int64_t mod_stride, int64_t mod_group,
+                              int norm_type, float eps, int dtype, void* stream);
+
+/*
+ * out = x * rsqrt(mean(x^2) + eps) * weight, per row.
+ * Replaces joyomni_ops::rmsnorm (deploy/joyomni_ops/csrc/rmsnorm.cu:76-95).
+ * x: [M, N] with row stride x_stride; out: [M, N] dense; weight [N] (x's dtype).
+ */
+int jo_rmsnorm(void* out, const void* x, const void* weight, int64_t M, int64_t N,
+               int64_t x_stride, float eps, int dtype, void* stream);
+
+/*
+ * Dynamic per-token FP8 e4m3 quantisation:
+ *   s[m] = max|x[m,:]| / 448 ; q = e4m3_satfinite_rn(clamp(x * (s ? 1/s : 0), +-448)).
+ * Replaces joyomni_ops::sgl_per_token_quant_fp8
+ *   (deploy/joyomni_ops/csrc/per_token_quant_fp8.cu:148-176).  Bit-exact.
+ * input: bf16/fp16 [M, K] contiguous, K % 4 == 0.  out_q: e4m3 [M, K]; out_s: fp32 [M].
+ */
+int jo_per_token_quant_fp8(const void* input, int in_dtype, void* out_q, float* out_s,
+                           int64_t M, int64_t K, void* stream);
+
+/*
+ * New fused entry (no reference counterpart; it composes
+ * fused_norm_scale_shift.cu:69-143 with per_token_quant_fp8.cu:43-83 as the
+ * reference model does in deploy/xvideo/models/dit/dit.py:351-357 ->
+ * fp8_linear.py:143-167): y = Norm(x)*(1+scale)+shift rounded to x's dtype,
+ * then per-token FP8 quantisation of y.  Arguments as jo_fused_norm_scale_shift
+ * (x dense) plus out_q e4m3 [M, N] and out_s fp32 [M].  dtype: F16/BF16.
+ */
+int jo_norm_modulate_quant_fp8(const void* x, const void* gamma, const void* beta,
+                               const void* scale, const void* shift, int64_t M, int64_t N,
+                               int64_t mod_stride, int64_t mod_group, int norm_type, float eps,
+                               int dtype, void* out_q, float* out_s, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JOYOMNI_B200_H_ */

@@ -1,0 +1,117 @@
+// Shared plumbing for the joyomni_b200 C-ABI library: status codes, the
+// thread-local last-error string, dtype tags and 16-byte vector helpers.
+//
+// Error convention (mirrors the reference's TORCH_CHECK / JO_CHECK_* behaviour,
+// deploy/joyomni_ops/include/joyomni_ops.h:8-15): every entry point validates
+// its arguments, returns a negative status on failure and leaves a message in
+// jo_last_error().  The Python shim turns JO_ERR_ARCH into NotImplementedError
+// (as TORCH_CHECK_NOT_IMPLEMENTED does, fp8_gemm.cu:1531) and everything else
+// into RuntimeError.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "../../include/joyomni_b200.h"
+
+namespace jo {
+
+// ---------------------------------------------------------------- errors ----
+void set_error(const char* fmt, ...);
+
+#define JO_REQUIRE(cond, code, ...)      \
+  do {                                   \
+    if (!(cond)) {                       \
+      ::jo::set_error(__VA_ARGS__);      \
+      return (code);                     \
+    }                                    \
+  } while (0)
+
+// Checks that the current device is sm_100 (B200 class).  Cached per device.
+int require_sm100();
+
+// Checks the last launch; converts a CUDA error into JO_ERR_CUDA.
+int check_launch(const char* what);
+
+// Number of SMs of the current device (cached).
+int sm_count();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// ------------------------------------------------------------- dtypes ------
+template <int DT> struct Elem;
+template <> struct Elem<JO_DTYPE_F32> { using T = float; };
+template <> struct Elem<JO_DTYPE_F16> { using T = __half; };
+template <> struct Elem<JO_DTYPE_BF16> { using T = __nv_bfloat16; };
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// A 16-byte vector of elements of T (8 x bf16/fp16 or 4 x fp32).
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  uint4 raw;
+  __device__ __forceinline__ float get(int i) const {
+    const T* p = reinterpret_cast<const T*>(&raw);
+    return to_f32(p[i]);
+  }
+  __device__ __forceinline__ void set(int i, float v) {
+    T* p = reinterpret_cast<T*>(&raw);
+    p[i] = from_f32<T>(v);
+  }
+};
+
+// Streaming 16-byte global load that does not allocate in L1 (single-use data).
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+// Plain 16-byte read-only load, cached in L1 (small reused tables).
+__device__ __forceinline__ uint4 ld_cached(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v, int width = 32) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) v += __shfl_xor_sync(0xffffffffu, v, o, 32);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o, 32));
+  return v;
+}
+
+constexpr float kFp8Max = 448.0f;
+
+// Two floats -> two packed e4m3 codes, round-to-nearest-even, satfinite.
+__device__ __forceinline__ uint16_t pack_e4m3x2(float lo, float hi) {
+  __nv_fp8x2_storage_t s = __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+  return static_cast<uint16_t>(s);
+}
+
+}  // namespace jo

@@ -108,6 +108,43 @@ __device__ __forceinline__ float warp_max(float v) {
 
 constexpr float kFp8Max = 448.0f;
 
+// ---- packed 16-bit pairs ---------------------------------------------------
+// One 32-bit word holds two 16-bit elements; element 0 in the low half.
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t w);
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  return __half22float2(h);
+}
+template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Bit pattern of +inf for the 16-bit type; |x| bit patterns above it are NaN.
+template <typename T> struct Bits16;
+template <> struct Bits16<__nv_bfloat16> { static constexpr uint32_t kInf = 0x7f80u; };
+template <> struct Bits16<__half> { static constexpr uint32_t kInf = 0x7c00u; };
+template <typename T> __device__ __forceinline__ float from_bits16(uint32_t b);
+template <> __device__ __forceinline__ float from_bits16<__nv_bfloat16>(uint32_t b) {
+  return __uint_as_float(b << 16);
+}
+template <> __device__ __forceinline__ float from_bits16<__half>(uint32_t b) {
+  return __half2float(__ushort_as_half((unsigned short)b));
+}
+// Running max of |elements| over packed pairs, on the integer bit patterns
+// (for non-NaN values |x| orders like its bits; NaN patterns sort above inf).
+__device__ __forceinline__ uint32_t absmax2(uint32_t acc, uint32_t w) { return __vmaxu2(acc, w & 0x7fff7fffu); }
+__device__ __forceinline__ uint32_t absmax2_fold(uint32_t acc) { return max(acc & 0xffffu, acc >> 16); }
+
 // Two floats -> two packed e4m3 codes, round-to-nearest-even, satfinite.
 __device__ __forceinline__ uint16_t pack_e4m3x2(float lo, float hi) {
   __nv_fp8x2_storage_t s = __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);

@@ -9,13 +9,13 @@
 //                               activation dtype -> per-token e4m3 quantisation
 //
 // Design (B200): every row is read from HBM exactly once with 16-byte
-// coalesced, L1-bypassing loads into registers, reduced by a "team" of TEAM
+// coalesced, L1-bypassing loads into registers, reduced by a "team" of
 // threads (warp shuffles; shared memory only when a team spans warps), then
-// written once with streaming stores.  Small per-column tables (gamma, beta,
-// weight, broadcast shift/scale) go through the read-only L1 path and are shared
-// by all rows an SM processes.  The team size is chosen per row length so that
-// each thread holds up to VPL 16-byte vectors in flight; for the headline
-// shape (N = 5120 bf16) that is 2 warps per row, 10 vectors per thread.
+// written once with streaming stores.  The grid is persistent and each thread
+// keeps the same columns for every row it handles, so per-column tables sit
+// in shared memory once per CTA and the next row is prefetched while the
+// current one is processed.  The broadcast-modulation and quantisation paths
+// at N >= 1024 use the deeper cp.async-staged kernel in row_staged.cu.
 //
 // Numerics follow the reference kernels operation for operation (fp32 math,
 // IEEE division for mean and scale, rsqrtf, the same product grouping, RNE
@@ -24,6 +24,9 @@
 #include "jo_common.cuh"
 
 namespace jo {
+int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, const void* gamma, const void* beta,
+                       const void* scale, const void* shift, uint8_t* q, float* s, int64_t M, int N, float eps,
+                       cudaStream_t st);
 namespace {
 
 enum RowOp : int { OP_NORM_MOD = 0, OP_RMSNORM = 1, OP_QUANT = 2, OP_NORM_MOD_QUANT = 3 };
@@ -45,24 +48,24 @@ struct RowArgs {
   float eps;
 };
 
-// Sum (or max) over the TEAM threads that own one row.  Teams are aligned to
-// TEAM-thread boundaries; for TEAM > 32 partial results meet in shared memory.
-template <int TEAM, bool MAX>
-__device__ __forceinline__ float team_reduce(float v, float* red) {
-  constexpr int W = TEAM < 32 ? TEAM : 32;
-#pragma unroll
-  for (int o = W / 2; o > 0; o >>= 1) {
-    float t = __shfl_xor_sync(0xffffffffu, v, o, 32);
+// Reduction over the `team` threads that own one row.  Sub-warp teams
+// (team < 32, a power of two, aligned inside a warp) use xor shuffles only;
+// larger teams are whole warps of one CTA (one row per CTA) and meet in shared
+// memory.  `red` must be a slot not reused before the next __syncthreads of the
+// following reduction (callers alternate slot sets by row parity).
+template <bool MAX>
+__device__ __forceinline__ float team_reduce(float v, int team, float* red) {
+  const int width = team < 32 ? team : 32;
+  for (int o = width >> 1; o > 0; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, v, o, 32);
     v = MAX ? fmaxf(v, t) : v + t;
   }
-  if constexpr (TEAM > 32) {
+  if (team > 32) {
     const int warp = threadIdx.x >> 5;
     if ((threadIdx.x & 31) == 0) red[warp] = v;
     __syncthreads();
-    const int first = (threadIdx.x / TEAM) * (TEAM / 32);
-    v = red[first];
-#pragma unroll
-    for (int w = 1; w < TEAM / 32; ++w) v = MAX ? fmaxf(v, red[first + w]) : v + red[first + w];
+    v = red[0];
+    for (int w = 1; w < (team >> 5); ++w) v = MAX ? fmaxf(v, red[w]) : v + red[w];
   }
   return v;
 }
@@ -74,178 +77,247 @@ __device__ __forceinline__ float quant_val(float x, float inv) {
   return fmaxf(fminf(v, kFp8Max), -kFp8Max);
 }
 
-template <typename T, int OP, int NORM, int TEAM, int VPL>
-__global__ void __launch_bounds__(TEAM > 256 ? TEAM : 256)
-    row_kernel(const RowArgs a) {
-  constexpr int CTA = TEAM > 256 ? TEAM : 256;
-  constexpr int ROWS = CTA / TEAM;
-  constexpr int VEC = 16 / sizeof(T);
-  __shared__ float red[3][CTA / 32];
+template <typename T, int VPL>
+__device__ __forceinline__ void load_vecs(Vec16<T> (&v)[VPL], const char* base, int tl, int team, int nvec,
+                                          bool ok, bool stream) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int idx = i * team + tl;
+    if (ok && idx < nvec)
+      v[i].raw = stream ? ld_stream(base + (int64_t)idx * 16) : ld_cached(base + (int64_t)idx * 16);
+    else
+      v[i].raw = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename T, int VPL>
+__device__ __forceinline__ void store_codes(const Vec16<T> (&v)[VPL], uint8_t* qr, int tl, int team, int nvec,
+                                            float inv) {
+  constexpr int VEC = Vec16<T>::N;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int idx = i * team + tl;
+    if (idx < nvec) {
+      uint32_t w[VEC / 4];
+#pragma unroll
+      for (int j = 0; j < VEC; j += 4) {
+        const uint32_t lo = pack_e4m3x2(quant_val(v[i].get(j), inv), quant_val(v[i].get(j + 1), inv));
+        const uint32_t hi = pack_e4m3x2(quant_val(v[i].get(j + 2), inv), quant_val(v[i].get(j + 3), inv));
+        w[j / 4] = lo | (hi << 16);
+      }
+      if constexpr (VEC == 8) {
+        asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(qr + (int64_t)idx * 8), "r"(w[0]), "r"(w[1])
+                     : "memory");
+      } else {
+        asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(qr + (int64_t)idx * 4), "r"(w[0]) : "memory");
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 lds16(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"((unsigned)__cvta_generic_to_shared(p)));
+  return r;
+}
+
+// Persistent, column-stationary row kernel.  A team of `team` threads owns a
+// row; thread tl of the team always handles the 16-byte vectors tl, tl+team,
+// ... of every row it processes.  Per-column tables (gamma, beta, rmsnorm
+// weight and, for a broadcast modulation vector, shift and scale) are staged
+// once per CTA in shared memory.  Per-row or grouped modulation rows are
+// loaded alongside x.  The next row (x and its modulation rows) is prefetched
+// into a second register set while the current row is reduced and written.
+template <typename T, int OP, int NORM, int VPL, bool MODROW>
+__global__ void __launch_bounds__(256, 2) row_kernel(const RowArgs a, const int team, const int rows_per_cta) {
+  constexpr int VEC = Vec16<T>::N;
+  constexpr bool HAS_MOD = (OP == OP_NORM_MOD || OP == OP_NORM_MOD_QUANT);
+  constexpr bool MOD_SMEM = HAS_MOD && !MODROW;
+  __shared__ float red[2][3][8];
+  extern __shared__ uint4 tab[];
 
   const int tid = threadIdx.x;
-  const int tl = tid % TEAM;
-  const int64_t row = (int64_t)blockIdx.x * ROWS + tid / TEAM;
-  const bool valid = row < a.M;
+  const int tl = tid % team;
+  const int tsub = tid / team;
   const int N = a.N;
   const int nvec = N / VEC;
+  const int64_t M = a.M;
+  const int64_t stride = (int64_t)gridDim.x * rows_per_cta;
+  const int64_t xrow_bytes = a.x_stride * (int64_t)sizeof(T);
+  const int64_t mrow_bytes = a.mod_stride * (int64_t)sizeof(T);
+  const char* xb = static_cast<const char*>(a.x);
+  const bool mod_stream = a.mod_group == 1;
 
-  Vec16<T> v[VPL];
+  // ---- shared-memory tables: [gamma][beta][scale][shift], nvec vectors each --
+  const bool has_g = (OP != OP_QUANT) && a.gamma != nullptr;
+  const bool has_b = (NORM == JO_NORM_LAYER && HAS_MOD) && has_g && a.beta != nullptr;
+  const uint4* tg = tab;
+  const uint4* tb = tab + nvec;
+  const uint4* tsc = tab + 2 * nvec;
+  const uint4* tsh = tab + 3 * nvec;
+  if constexpr (OP != OP_QUANT) {
+    for (int i = tid; i < nvec; i += blockDim.x) {
+      uint4* t = tab;
+      if (has_g) t[i] = ld_cached(static_cast<const char*>(a.gamma) + (int64_t)i * 16);
+      if (has_b) t[nvec + i] = ld_cached(static_cast<const char*>(a.beta) + (int64_t)i * 16);
+      if constexpr (MOD_SMEM) {
+        t[2 * nvec + i] = ld_cached(static_cast<const char*>(a.scale) + (int64_t)i * 16);
+        t[3 * nvec + i] = ld_cached(static_cast<const char*>(a.shift) + (int64_t)i * 16);
+      }
+    }
+    __syncthreads();
+  }
+
+  Vec16<T> SC[MODROW ? VPL : 1], SH[MODROW ? VPL : 1];
+  Vec16<T> SCn[MODROW ? VPL : 1], SHn[MODROW ? VPL : 1];
+  auto mod_base = [&](const void* p, int64_t row) {
+    return static_cast<const char*>(p) + (row / a.mod_group) * mrow_bytes;
+  };
+
+  // ---- prologue: first row ------------------------------------------------
+  int64_t base = (int64_t)blockIdx.x * rows_per_cta;
+  Vec16<T> X[VPL], XN[VPL];
   {
-    const char* xr = static_cast<const char*>(a.x) + (valid ? row : 0) * a.x_stride * (int64_t)sizeof(T);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int idx = i * TEAM + tl;
-      v[i].raw = (valid && idx < nvec) ? ld_stream(xr + (int64_t)idx * 16) : make_uint4(0, 0, 0, 0);
+    const int64_t row = base + tsub;
+    const bool ok = row < M;
+    load_vecs<T, VPL>(X, xb + (ok ? row : 0) * xrow_bytes, tl, team, nvec, ok, true);
+    if constexpr (MODROW) {
+      load_vecs<T, VPL>(SC, mod_base(a.scale, ok ? row : 0), tl, team, nvec, ok, mod_stream);
+      load_vecs<T, VPL>(SH, mod_base(a.shift, ok ? row : 0), tl, team, nvec, ok, mod_stream);
     }
   }
 
-  if constexpr (OP == OP_QUANT) {
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i)
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) amax = fmaxf(amax, fabsf(v[i].get(j)));
-    amax = team_reduce<TEAM, true>(amax, red[0]);
-    const float s = amax / kFp8Max;
-    if (valid && tl == 0) a.s[row] = s;
-    const float inv = quant_inv(s);
-    uint8_t* qr = a.q + (valid ? row : 0) * (int64_t)N;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int idx = i * TEAM + tl;
-      if (valid && idx < nvec) {
-        uint32_t w[VEC / 4];
-#pragma unroll
-        for (int j = 0; j < VEC; j += 4) {
-          uint32_t lo = pack_e4m3x2(quant_val(v[i].get(j), inv), quant_val(v[i].get(j + 1), inv));
-          uint32_t hi = pack_e4m3x2(quant_val(v[i].get(j + 2), inv), quant_val(v[i].get(j + 3), inv));
-          w[j / 4] = lo | (hi << 16);
-        }
-        if constexpr (VEC == 8) {
-          asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(qr + (int64_t)idx * 8), "r"(w[0]), "r"(w[1])
-                       : "memory");
-        } else {
-          asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(qr + (int64_t)idx * 4), "r"(w[0]) : "memory");
-        }
+  int parity = 0;
+  for (; base < M; base += stride, parity ^= 1) {
+    const int64_t row = base + tsub;
+    const bool valid = row < M;
+    {  // prefetch the next row of this team
+      const int64_t nrow = row + stride;
+      const bool nok = nrow < M;
+      load_vecs<T, VPL>(XN, xb + (nok ? nrow : 0) * xrow_bytes, tl, team, nvec, nok, true);
+      if constexpr (MODROW) {
+        load_vecs<T, VPL>(SCn, mod_base(a.scale, nok ? nrow : 0), tl, team, nvec, nok, mod_stream);
+        load_vecs<T, VPL>(SHn, mod_base(a.shift, nok ? nrow : 0), tl, team, nvec, nok, mod_stream);
       }
     }
-    return;
-  } else {
-    // ---- statistics -----------------------------------------------------
-    float mean = 0.f, r;
-    if constexpr (NORM == JO_NORM_LAYER) {
-      float sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i)
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) sum += v[i].get(j);
-      sum = team_reduce<TEAM, false>(sum, red[0]);
-      mean = sum / (float)N;
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        if (i * TEAM + tl < nvec) {
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) {
-            const float d = v[i].get(j) - mean;
-            ss = fmaf(d, d, ss);
-          }
-        }
-      }
-      ss = team_reduce<TEAM, false>(ss, red[1]);
-      r = rsqrtf(ss / (float)N + a.eps);
-    } else {
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i)
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) ss = fmaf(v[i].get(j), v[i].get(j), ss);
-      ss = team_reduce<TEAM, false>(ss, red[0]);
-      r = rsqrtf(ss / (float)N + a.eps);
-    }
+    float* rs = red[parity][0];
 
-    // ---- elementwise ----------------------------------------------------
-    const char* g = static_cast<const char*>(a.gamma);
-    const char* b = static_cast<const char*>(a.beta);
-    const char* scr = nullptr;
-    const char* shr = nullptr;
-    bool mod_stream = false;
-    if constexpr (OP != OP_RMSNORM) {
-      const int64_t mrow = (valid ? row : 0) / a.mod_group;
-      scr = static_cast<const char*>(a.scale) + mrow * a.mod_stride * (int64_t)sizeof(T);
-      shr = static_cast<const char*>(a.shift) + mrow * a.mod_stride * (int64_t)sizeof(T);
-      mod_stream = (a.mod_group == 1 && a.mod_stride != 0);
-    }
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int idx = i * TEAM + tl;
-      if (!(valid && idx < nvec)) continue;
-      const int64_t off = (int64_t)idx * 16;
-      if constexpr (OP == OP_RMSNORM) {
-        Vec16<T> w;
-        w.raw = ld_cached(g + off);
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) v[i].set(j, v[i].get(j) * r * w.get(j));
-      } else {
-        Vec16<T> gv, bv, sc, sh;
-        if (g) gv.raw = ld_cached(g + off);
-        if (NORM == JO_NORM_LAYER && g && b) bv.raw = ld_cached(b + off);
-        sc.raw = mod_stream ? ld_stream(scr + off) : ld_cached(scr + off);
-        sh.raw = mod_stream ? ld_stream(shr + off) : ld_cached(shr + off);
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          float t;
-          if constexpr (NORM == JO_NORM_LAYER) {
-            const float gj = g ? gv.get(j) : 1.f;
-            const float bj = (g && b) ? bv.get(j) : 0.f;
-            t = ((v[i].get(j) - mean) * r * gj + bj) * (1.f + sc.get(j)) + sh.get(j);
-          } else {
-            const float gj = g ? gv.get(j) : 1.f;
-            t = (v[i].get(j) * r * gj) * (1.f + sc.get(j)) + sh.get(j);
-          }
-          v[i].set(j, t);  // rounds to T (RNE), as the reference's T(float) store
-        }
-      }
-    }
-
-    if constexpr (OP == OP_NORM_MOD || OP == OP_RMSNORM) {
-      char* yr = static_cast<char*>(a.y) + (valid ? row : 0) * (int64_t)N * (int64_t)sizeof(T);
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int idx = i * TEAM + tl;
-        if (valid && idx < nvec) st_stream(yr + (int64_t)idx * 16, v[i].raw);
-      }
-    } else {
-      // OP_NORM_MOD_QUANT: quantise the rounded y row exactly as the reference
-      // per-token kernel would quantise the bf16/fp16 tensor written by
-      // fused_norm_scale_shift.
+    if constexpr (OP == OP_QUANT) {
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        if (i * TEAM + tl < nvec) {
+      for (int i = 0; i < VPL; ++i)
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) amax = fmaxf(amax, fabsf(v[i].get(j)));
+        for (int j = 0; j < VEC; ++j) amax = fmaxf(amax, fabsf(X[i].get(j)));
+      amax = team_reduce<true>(amax, team, rs);
+      const float s = amax / kFp8Max;
+      if (valid) {
+        if (tl == 0) a.s[row] = s;
+        store_codes<T, VPL>(X, a.q + row * (int64_t)N, tl, team, nvec, quant_inv(s));
+      }
+    } else {
+      // ---- statistics -----------------------------------------------------
+      float mean = 0.f, r;
+      if constexpr (NORM == JO_NORM_LAYER) {
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) sum += X[i].get(j);
+        sum = team_reduce<false>(sum, team, rs);
+        mean = sum / (float)N;
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          if (i * team + tl < nvec) {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) {
+              const float d = X[i].get(j) - mean;
+              ss = fmaf(d, d, ss);
+            }
+          }
+        }
+        ss = team_reduce<false>(ss, team, red[parity][1]);
+        r = rsqrtf(ss / (float)N + a.eps);
+      } else {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) ss = fmaf(X[i].get(j), X[i].get(j), ss);
+        ss = team_reduce<false>(ss, team, rs);
+        r = rsqrtf(ss / (float)N + a.eps);
+      }
+      // ---- elementwise (in place in X, rounded to T) ----------------------
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int idx = i * team + tl;
+        if (idx >= nvec) continue;
+        Vec16<T> g, b, sc, sh;
+        if (has_g) g.raw = lds16(tg + idx);
+        if constexpr (OP == OP_RMSNORM) {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) X[i].set(j, X[i].get(j) * r * g.get(j));
+        } else {
+          if (has_b) b.raw = lds16(tb + idx);
+          if constexpr (MOD_SMEM) {
+            sc.raw = lds16(tsc + idx);
+            sh.raw = lds16(tsh + idx);
+          } else {
+            sc = SC[i];
+            sh = SH[i];
+          }
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            float t;
+            const float gj = has_g ? g.get(j) : 1.f;
+            if constexpr (NORM == JO_NORM_LAYER) {
+              const float bj = has_b ? b.get(j) : 0.f;
+              t = ((X[i].get(j) - mean) * r * gj + bj) * (1.f + sc.get(j)) + sh.get(j);
+            } else {
+              t = (X[i].get(j) * r * gj) * (1.f + sc.get(j)) + sh.get(j);
+            }
+            X[i].set(j, t);  // RNE to T, as the reference's T(float) store
+          }
         }
       }
-      amax = team_reduce<TEAM, true>(amax, red[2]);
-      const float s = amax / kFp8Max;
-      if (valid && tl == 0) a.s[row] = s;
-      const float inv = quant_inv(s);
-      uint8_t* qr = a.q + (valid ? row : 0) * (int64_t)N;
+      if constexpr (OP == OP_NORM_MOD || OP == OP_RMSNORM) {
+        if (valid) {
+          char* yr = static_cast<char*>(a.y) + row * (int64_t)N * (int64_t)sizeof(T);
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const int idx = i * team + tl;
+            if (idx < nvec) st_stream(yr + (int64_t)idx * 16, X[i].raw);
+          }
+        }
+      } else {
+        // OP_NORM_MOD_QUANT: quantise the rounded row exactly as the reference
+        // per-token kernel quantises the tensor fused_norm_scale_shift wrote.
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          if (i * team + tl < nvec) {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) amax = fmaxf(amax, fabsf(X[i].get(j)));
+          }
+        }
+        amax = team_reduce<true>(amax, team, red[parity][2]);
+        const float s = amax / kFp8Max;
+        if (valid) {
+          if (tl == 0) a.s[row] = s;
+          store_codes<T, VPL>(X, a.q + row * (int64_t)N, tl, team, nvec, quant_inv(s));
+        }
+      }
+    }
+    // rotate the prefetched row into place
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) X[i] = XN[i];
+    if constexpr (MODROW) {
 #pragma unroll
       for (int i = 0; i < VPL; ++i) {
-        const int idx = i * TEAM + tl;
-        if (valid && idx < nvec) {
-          uint32_t w[2];
-#pragma unroll
-          for (int j = 0; j < 8; j += 4) {
-            uint32_t lo = pack_e4m3x2(quant_val(v[i].get(j), inv), quant_val(v[i].get(j + 1), inv));
-            uint32_t hi = pack_e4m3x2(quant_val(v[i].get(j + 2), inv), quant_val(v[i].get(j + 3), inv));
-            w[j / 4] = lo | (hi << 16);
-          }
-          asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(qr + (int64_t)idx * 8), "r"(w[0]), "r"(w[1])
-                       : "memory");
-        }
+        SC[i] = SCn[i];
+        SH[i] = SHn[i];
       }
     }
   }
@@ -352,42 +424,79 @@ inline int pow2ceil(int v) {
   return p;
 }
 
-template <typename T, int OP, int NORM, int TEAM, int VPL>
-void launch_team(const RowArgs& a, cudaStream_t st) {
-  constexpr int CTA = TEAM > 256 ? TEAM : 256;
-  constexpr int ROWS = CTA / TEAM;
-  const int64_t grid = (a.M + ROWS - 1) / ROWS;
-  row_kernel<T, OP, NORM, TEAM, VPL><<<(unsigned)grid, CTA, 0, st>>>(a);
+// Persistent grid: as many CTAs as fit on the device (occupancy API, cached per
+// kernel instance, CTA size and shared-memory size), capped by the work.
+template <typename T, int OP, int NORM, int VPL, bool MODROW>
+void launch_rows(const RowArgs& a, int team, cudaStream_t st) {
+  const int cta = team >= 32 ? team : 256;
+  const int rows_per_cta = cta / team;
+  const int nvec = a.N / (16 / (int)sizeof(T));
+  const int ntab = OP == OP_QUANT ? 0 : (MODROW || OP == OP_RMSNORM) ? 2 : 4;
+  const size_t smem = (size_t)ntab * nvec * 16;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(row_kernel<T, OP, NORM, VPL, MODROW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         16 * 2048 * 4);
+    attr_set = true;
+  }
+  static int cached_cta = -1, cached_blocks = 0;
+  static size_t cached_smem = 0;
+  if (cached_cta != cta || cached_smem != smem) {
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_kernel<T, OP, NORM, VPL, MODROW>, cta, smem);
+    cached_blocks = (per_sm > 0 ? per_sm : 1) * sm_count();
+    cached_cta = cta;
+    cached_smem = smem;
+  }
+  const int64_t need = (a.M + rows_per_cta - 1) / rows_per_cta;
+  const int64_t grid = need < cached_blocks ? need : cached_blocks;
+  row_kernel<T, OP, NORM, VPL, MODROW><<<(unsigned)grid, cta, smem, st>>>(a, team, rows_per_cta);
 }
 
-// Picks the team geometry for a row of nvec 16-byte vectors.
+// Team geometry for a row of nvec 16-byte vectors: VPL vectors per thread
+// (4 preferred), team = whole warps spanning the row (at most 256 threads), or
+// a power-of-two sub-warp team for short rows.  Longer rows take the scalar path.
+inline bool pick_team(int nvec, int& vpl, int& team) {
+  if (nvec <= 8) {
+    vpl = 2;
+    team = pow2ceil((nvec + 1) / 2);
+    return true;
+  }
+  for (int v : {4, 8}) {
+    int t = (nvec + v - 1) / v;
+    t = t <= 16 ? pow2ceil(t) : (t + 31) / 32 * 32;
+    if (t <= 256) {
+      vpl = v;
+      team = t;
+      return true;
+    }
+  }
+  return false;
+}
+
 template <typename T, int OP, int NORM>
 int dispatch(const RowArgs& a, bool vec_ok, cudaStream_t st, const char* what) {
   if (a.M == 0) return JO_OK;
   constexpr int VEC = 16 / sizeof(T);
   const int nvec = a.N / VEC;
-  if (!vec_ok || nvec > 16 * 1024) {
+  int vpl = 0, team = 0;
+  if (!vec_ok || !pick_team(nvec, vpl, team)) {
     row_kernel_scalar<T, OP, NORM><<<(unsigned)a.M, 256, 0, st>>>(a);
     return check_launch(what);
   }
-  if (nvec <= 64) {
-    const int team = pow2ceil((nvec + 3) / 4);
-    if (team <= 4) launch_team<T, OP, NORM, 4, 4>(a, st);
-    else if (team <= 8) launch_team<T, OP, NORM, 8, 4>(a, st);
-    else launch_team<T, OP, NORM, 16, 4>(a, st);
-  } else {
-    int team = pow2ceil((nvec + 15) / 16);
-    if (team < 8) team = 8;
-    switch (team) {
-      case 8: launch_team<T, OP, NORM, 8, 16>(a, st); break;
-      case 16: launch_team<T, OP, NORM, 16, 16>(a, st); break;
-      case 32: launch_team<T, OP, NORM, 32, 16>(a, st); break;
-      case 64: launch_team<T, OP, NORM, 64, 16>(a, st); break;
-      case 128: launch_team<T, OP, NORM, 128, 16>(a, st); break;
-      case 256: launch_team<T, OP, NORM, 256, 16>(a, st); break;
-      case 512: launch_team<T, OP, NORM, 512, 16>(a, st); break;
-      default: launch_team<T, OP, NORM, 1024, 16>(a, st); break;
+  // Modulation rows that change along M are loaded with x; a single broadcast
+  // vector is staged in shared memory.
+  const bool modrow = (OP == OP_NORM_MOD || OP == OP_NORM_MOD_QUANT) && a.mod_stride != 0 && a.mod_group < a.M;
+  if (modrow) {
+    if constexpr (OP == OP_NORM_MOD || OP == OP_NORM_MOD_QUANT) {
+      if (vpl == 2) launch_rows<T, OP, NORM, 2, true>(a, team, st);
+      else if (vpl == 4) launch_rows<T, OP, NORM, 4, true>(a, team, st);
+      else launch_rows<T, OP, NORM, 8, true>(a, team, st);
     }
+  } else {
+    if (vpl == 2) launch_rows<T, OP, NORM, 2, false>(a, team, st);
+    else if (vpl == 4) launch_rows<T, OP, NORM, 4, false>(a, team, st);
+    else launch_rows<T, OP, NORM, 8, false>(a, team, st);
   }
   return check_launch(what);
 }
@@ -441,6 +550,11 @@ int jo_fused_norm_scale_shift(void* y, const void* x, const void* gamma, const v
                       (!gamma || aligned16(gamma)) && (!beta || aligned16(beta)) && ((N * es) % 16 == 0) &&
                       ((x_stride * es) % 16 == 0) && ((mod_stride * es) % 16 == 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool broadcast = (mod_stride == 0 || mod_group >= M) && x_stride == N;
+  if (vec_ok && broadcast &&
+      staged_rows_launch(OP_NORM_MOD, norm_type, dtype, x, y, gamma, beta, scale, shift, nullptr, nullptr, M,
+                         (int)N, eps, s) == JO_OK)
+    return check_launch(what);
   return norm_type == JO_NORM_LAYER ? dispatch_dtype<OP_NORM_MOD, JO_NORM_LAYER>(dtype, a, vec_ok, s, what)
                                     : dispatch_dtype<OP_NORM_MOD, JO_NORM_RMS>(dtype, a, vec_ok, s, what);
 }
@@ -482,6 +596,9 @@ int jo_per_token_quant_fp8(const void* input, int in_dtype, void* out_q, float* 
   RowArgs a{input, K, nullptr, nullptr, nullptr, nullptr, nullptr, 0, 1,
             static_cast<uint8_t*>(out_q), out_s, M, (int)K, 0.f};
   const bool vec_ok = aligned16(input) && aligned8(out_q) && (K % 8) == 0;
+  if (vec_ok && staged_rows_launch(OP_QUANT, JO_NORM_RMS, in_dtype, input, nullptr, nullptr, nullptr, nullptr,
+                                   nullptr, static_cast<uint8_t*>(out_q), out_s, M, (int)K, 0.f, s) == JO_OK)
+    return check_launch(what);
   return dispatch_dtype<OP_QUANT, JO_NORM_RMS>(in_dtype, a, vec_ok, s, what);
 }
 
@@ -511,6 +628,11 @@ int jo_norm_modulate_quant_fp8(const void* x, const void* gamma, const void* bet
   const bool vec_ok = aligned16(x) && aligned8(out_q) && aligned16(scale) && aligned16(shift) &&
                       (!gamma || aligned16(gamma)) && (!beta || aligned16(beta)) && (N % 8) == 0 &&
                       ((mod_stride * 2) % 16 == 0);
+  const bool broadcast = mod_stride == 0 || mod_group >= M;
+  if (vec_ok && broadcast &&
+      staged_rows_launch(OP_NORM_MOD_QUANT, norm_type, dtype, x, nullptr, gamma, beta, scale, shift,
+                         static_cast<uint8_t*>(out_q), out_s, M, (int)N, eps, s) == JO_OK)
+    return check_launch(what);
   return norm_type == JO_NORM_LAYER ? dispatch_dtype<OP_NORM_MOD_QUANT, JO_NORM_LAYER>(dtype, a, vec_ok, s, what)
                                     : dispatch_dtype<OP_NORM_MOD_QUANT, JO_NORM_RMS>(dtype, a, vec_ok, s, what);
 }

@@ -1,0 +1,511 @@
+// Staged (deep-pipelined) row kernel for the bandwidth-critical broadcast-
+// modulation paths: the fused norm -> modulate -> per-token FP8 entry, the
+// broadcast norm -> modulate, and plain per-token quantisation (N >= 1024).
+//
+// Why a second kernel: with a register-resident row the number of rows in
+// flight per SM is bounded by registers (about 3 rows of 10 KB at N = 5120),
+// which leaves HBM latency exposed.  Here every thread streams its own 16-byte
+// pieces of the next rows of its team into shared memory with cp.async
+// (L1-bypassing), so rows are in flight without register cost and without a
+// CTA barrier: a thread only ever reads back the pieces it copied itself
+// (visible after cp.async.wait_group).  A team processes R rows per iteration
+// so that the per-row fixed work (reductions, divisions, address set-up) and
+// the column-table reads are shared by R rows, and warps carry R independent
+// dependency chains.
+//
+// Layout in shared memory (dynamic):
+//   float tables[ntab][N]           gamma, (beta), 1 + scale, shift in fp32, staged once
+//   uint4 ring[TEAMS][S][R][nvec]   per-team ring of S stages of R rows
+// Teams are `team` threads (whole warps); a CTA holds TEAMS teams that
+// synchronise among themselves with named barriers (id 1 + team index).
+//
+// Numerics equal row_ops.cu (and the reference kernels): (1 + scale) is formed
+// in fp32 exactly as the reference does per element, only earlier.  The per-
+// row absmax runs on the 16-bit bit patterns (exact for non-NaN values, and it
+// flags NaN/Inf rows); rows whose codes could involve NaN or Inf take the
+// reference's explicit-clamp form, all others rely on the identical satfinite
+// saturation of the e4m3 conversion.
+#include "jo_common.cuh"
+
+namespace jo {
+namespace staged {
+
+enum : int { OP_NORM_MOD = 0, OP_QUANT = 2, OP_NORM_MOD_QUANT = 3 };
+
+struct Args {
+  const void* x;
+  void* y;            // OP_NORM_MOD output [M, N]
+  const void* gamma;  // [N] or null
+  const void* beta;   // [N] or null (layer norm, with gamma)
+  const void* scale;  // [N] broadcast
+  const void* shift;  // [N] broadcast
+  uint8_t* q;
+  float* s;
+  int64_t M;
+  int N;
+  float eps;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void team_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ uint4 lds16(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"((unsigned)__cvta_generic_to_shared(p)));
+  return r;
+}
+__device__ __forceinline__ float4 lds16f(const float* p) {
+  float4 r;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "r"((unsigned)__cvta_generic_to_shared(p)));
+  return r;
+}
+
+// Team-wide reductions of R independent values (one per row).  Warp shuffles
+// first; teams spanning several warps meet in shared memory behind a named
+// barrier.  `red` slots must not be reused before the next barrier of the
+// following reduction (callers alternate slot sets by iteration parity).
+template <int R>
+__device__ __forceinline__ void team_sum(float (&v)[R], int team, int bar_id, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] += __shfl_xor_sync(0xffffffffu, v[r], o, 32);
+  const int nw = team >> 5;
+  if (nw > 1) {
+    const int w = (threadIdx.x % team) >> 5;
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int r = 0; r < R; ++r) red[r * 16 + w] = v[r];
+    team_bar(bar_id, team);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float t = red[r * 16];
+      for (int i = 1; i < nw; ++i) t += red[r * 16 + i];
+      v[r] = t;
+    }
+  }
+}
+template <int R>
+__device__ __forceinline__ void team_fmax(float (&v)[R], int team, int bar_id, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = fmaxf(v[r], __shfl_xor_sync(0xffffffffu, v[r], o, 32));
+  const int nw = team >> 5;
+  if (nw > 1) {
+    const int w = (threadIdx.x % team) >> 5;
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int r = 0; r < R; ++r) red[r * 16 + w] = v[r];
+    team_bar(bar_id, team);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float t = red[r * 16];
+      for (int i = 1; i < nw; ++i) t = fmaxf(t, red[r * 16 + i]);
+      v[r] = t;
+    }
+  }
+}
+template <int R>
+__device__ __forceinline__ void team_umax(uint32_t (&v)[R], int team, int bar_id, float* red) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = __reduce_max_sync(0xffffffffu, v[r]);
+  const int nw = team >> 5;
+  if (nw > 1) {
+    uint32_t* rr = reinterpret_cast<uint32_t*>(red);
+    const int w = (threadIdx.x % team) >> 5;
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int r = 0; r < R; ++r) rr[r * 16 + w] = v[r];
+    team_bar(bar_id, team);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      uint32_t t = rr[r * 16];
+      for (int i = 1; i < nw; ++i) t = max(t, rr[r * 16 + i]);
+      v[r] = t;
+    }
+  }
+}
+
+__device__ __forceinline__ float qval(float x, float inv) {
+  const float v = __fmul_rn(x, inv);
+  return fmaxf(fminf(v, kFp8Max), -kFp8Max);
+}
+
+// Codes of one 16-byte vector (8 elements in 4 words) -> 8 bytes.
+// FAST: x*inv is finite for every element (the row has no NaN/Inf and inv is
+// finite), so the e4m3 conversion's satfinite saturation equals the
+// reference's explicit clamp.  Otherwise the exact clamp form is used (it maps
+// NaN products to 448 as fminf/fmaxf do in the reference).
+template <typename T, bool FAST>
+__device__ __forceinline__ uint2 codes8(const uint4& v, float inv) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t c[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = unpack2<T>(w[k]);
+    if (FAST) c[k] = pack_e4m3x2(__fmul_rn(f.x, inv), __fmul_rn(f.y, inv));
+    else c[k] = pack_e4m3x2(qval(f.x, inv), qval(f.y, inv));
+  }
+  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+}
+
+__device__ __forceinline__ void st_cs8(void* p, uint2 v) {
+  asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+
+// Quantise R rows held in X (16-bit elements; bits[r] = team max of |x| as a
+// 16-bit pattern) and write codes + scales.
+template <typename T, int VPL, int R>
+__device__ __forceinline__ void quant_rows(const Vec16<T> (&X)[R][VPL], const uint32_t (&bits)[R],
+                                           const int64_t (&row)[R], const bool (&ok)[R], uint8_t* q, float* sout,
+                                           int N, int team, int tl, int bar_id, float* red_slow) {
+  const int nvec = N / 8;
+  float amax[R];
+  bool any_slow = false;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    amax[r] = from_bits16<T>(bits[r]);
+    any_slow |= !(bits[r] < Bits16<T>::kInf);
+  }
+  if (any_slow) {  // team-uniform: NaN or Inf in a row; reference amax ignores NaN (fmaxf)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i)
+        if (i * team + tl < nvec) {
+          const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack2<T>(w[k]);
+            m = fmaxf(m, fabsf(f.x));
+            m = fmaxf(m, fabsf(f.y));
+          }
+        }
+      amax[r] = m;
+    }
+    team_fmax<R>(amax, team, bar_id, red_slow);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float s = amax[r] / kFp8Max;
+    if (ok[r] && tl == 0) sout[row[r]] = s;
+    const float inv = s == 0.f ? 0.f : __frcp_rn(s);
+    const bool fast = (bits[r] < Bits16<T>::kInf) && inv < __int_as_float(0x7f800000);
+    if (!ok[r]) continue;
+    uint8_t* qr = q + row[r] * (int64_t)N;
+    if (fast) {
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int idx = i * team + tl;
+        if (idx < nvec) st_cs8(qr + (int64_t)idx * 8, codes8<T, true>(X[r][i].raw, inv));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int idx = i * team + tl;
+        if (idx < nvec) st_cs8(qr + (int64_t)idx * 8, codes8<T, false>(X[r][i].raw, inv));
+      }
+    }
+  }
+}
+
+template <typename T, int OP, int NORM, int VPL, int S, int R>
+__global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int team, const int teams) {
+  constexpr bool HAS_NORM = (OP != OP_QUANT);
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[15][2][4][R * 16];
+
+  const int N = a.N;
+  const int nvec = N / 8;
+  const int tid = threadIdx.x;
+  const int tm = tid / team;   // team in CTA
+  const int tl = tid % team;   // thread in team
+  const int bar_id = 1 + tm;
+
+  // ---- fp32 tables -------------------------------------------------------
+  constexpr int NTAB = HAS_NORM ? (NORM == JO_NORM_LAYER ? 4 : 3) : 0;
+  float* tg = reinterpret_cast<float*>(smem_raw);       // gamma
+  float* tsc = tg + N;                                  // 1 + scale
+  float* tsh = tsc + N;                                 // shift
+  float* tb = tsh + N;                                  // beta (layer norm only)
+  uint4* ring = reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) +
+                (size_t)tm * S * R * nvec;
+  if constexpr (HAS_NORM) {
+    const bool has_g = a.gamma != nullptr;
+    const bool has_b = NORM == JO_NORM_LAYER && has_g && a.beta != nullptr;
+    const T* g = static_cast<const T*>(a.gamma);
+    const T* b = static_cast<const T*>(a.beta);
+    const T* sc = static_cast<const T*>(a.scale);
+    const T* sh = static_cast<const T*>(a.shift);
+    for (int i = tid; i < N; i += blockDim.x) {
+      tg[i] = has_g ? to_f32(g[i]) : 1.f;
+      if (NORM == JO_NORM_LAYER) tb[i] = has_b ? to_f32(b[i]) : 0.f;
+      tsc[i] = 1.f + to_f32(sc[i]);
+      tsh[i] = to_f32(sh[i]);
+    }
+    __syncthreads();
+  }
+
+  const int64_t M = a.M;
+  const int64_t ngroups = (M + R - 1) / R;
+  const int64_t gteam = (int64_t)blockIdx.x * teams + tm;
+  const int64_t tstride = (int64_t)gridDim.x * teams;
+  const char* xb = static_cast<const char*>(a.x);
+  const int64_t rowb = (int64_t)N * sizeof(T);
+
+  auto issue = [&](int64_t grp, int stage) {
+    if (grp < ngroups) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int64_t row = grp * R + r;
+        if (row < M) {
+          const char* src = xb + row * rowb;
+          uint4* dst = ring + (size_t)(stage * R + r) * nvec;
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const int idx = i * team + tl;
+            if (idx < nvec) cp_async16(dst + idx, src + (int64_t)idx * 16);
+          }
+        }
+      }
+    }
+    cp_commit();
+  };
+
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) issue(gteam + s * tstride, s);
+
+  int stage = 0;
+  int parity = 0;
+  for (int64_t grp = gteam; grp < ngroups; grp += tstride, parity ^= 1) {
+    issue(grp + (int64_t)(S - 1) * tstride, (stage + S - 1) % S);
+    cp_wait<S - 1>();
+    Vec16<T> X[R][VPL];
+    int64_t row[R];
+    bool ok[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      row[r] = grp * R + r;
+      ok[r] = row[r] < M;
+      const uint4* src = ring + (size_t)(stage * R + r) * nvec;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int idx = i * team + tl;
+        X[r][i].raw = (ok[r] && idx < nvec) ? lds16(src + idx) : make_uint4(0, 0, 0, 0);
+      }
+    }
+    stage = (stage + 1 == S) ? 0 : stage + 1;
+
+    if constexpr (OP == OP_QUANT) {
+      uint32_t bits[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          acc = absmax2(acc, X[r][i].raw.x);
+          acc = absmax2(acc, X[r][i].raw.y);
+          acc = absmax2(acc, X[r][i].raw.z);
+          acc = absmax2(acc, X[r][i].raw.w);
+        }
+        bits[r] = absmax2_fold(acc);
+      }
+      team_umax<R>(bits, team, bar_id, red[tm][parity][0]);
+      quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[tm][parity][1]);
+    } else {
+      float mean[R], rr[R];
+      if constexpr (NORM == JO_NORM_LAYER) {
+        float sum[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          sum[r] = 0.f;
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack2<T>(w[k]);
+              sum[r] += f.x;
+              sum[r] += f.y;
+            }
+          }
+        }
+        team_sum<R>(sum, team, bar_id, red[tm][parity][0]);
+        float ss[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          mean[r] = sum[r] / (float)N;
+          ss[r] = 0.f;
+#pragma unroll
+          for (int i = 0; i < VPL; ++i)
+            if (i * team + tl < nvec) {
+              const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float2 f = unpack2<T>(w[k]);
+                const float d0 = f.x - mean[r], d1 = f.y - mean[r];
+                ss[r] = fmaf(d0, d0, ss[r]);
+                ss[r] = fmaf(d1, d1, ss[r]);
+              }
+            }
+        }
+        team_sum<R>(ss, team, bar_id, red[tm][parity][1]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
+      } else {
+        float ss[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          mean[r] = 0.f;
+          ss[r] = 0.f;
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack2<T>(w[k]);
+              ss[r] = fmaf(f.x, f.x, ss[r]);
+              ss[r] = fmaf(f.y, f.y, ss[r]);
+            }
+          }
+        }
+        team_sum<R>(ss, team, bar_id, red[tm][parity][0]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
+      }
+      uint32_t acc[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = 0;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int idx = i * team + tl;
+        if (idx >= nvec) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = idx * 8 + 4 * h;
+          const float4 g = lds16f(tg + c);
+          const float4 sc = lds16f(tsc + c);
+          const float4 sh = lds16f(tsh + c);
+          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+          if constexpr (NORM == JO_NORM_LAYER) b = lds16f(tb + c);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            uint32_t* wr = reinterpret_cast<uint32_t*>(&X[r][i].raw);
+            const float2 f0 = unpack2<T>(wr[2 * h]);
+            const float2 f1 = unpack2<T>(wr[2 * h + 1]);
+            const float m = mean[r], rv = rr[r];
+            float y0, y1, y2, y3;
+            if constexpr (NORM == JO_NORM_LAYER) {
+              y0 = ((f0.x - m) * rv * g.x + b.x) * sc.x + sh.x;
+              y1 = ((f0.y - m) * rv * g.y + b.y) * sc.y + sh.y;
+              y2 = ((f1.x - m) * rv * g.z + b.z) * sc.z + sh.z;
+              y3 = ((f1.y - m) * rv * g.w + b.w) * sc.w + sh.w;
+            } else {
+              y0 = (f0.x * rv * g.x) * sc.x + sh.x;
+              y1 = (f0.y * rv * g.y) * sc.y + sh.y;
+              y2 = (f1.x * rv * g.z) * sc.z + sh.z;
+              y3 = (f1.y * rv * g.w) * sc.w + sh.w;
+            }
+            wr[2 * h] = pack2<T>(y0, y1);      // RNE to T, as the reference's T(float) store
+            wr[2 * h + 1] = pack2<T>(y2, y3);
+            if constexpr (OP == OP_NORM_MOD_QUANT) {
+              acc[r] = absmax2(acc[r], wr[2 * h]);
+              acc[r] = absmax2(acc[r], wr[2 * h + 1]);
+            }
+          }
+        }
+      }
+      if constexpr (OP == OP_NORM_MOD) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if (!ok[r]) continue;
+          char* yr = static_cast<char*>(a.y) + row[r] * rowb;
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const int idx = i * team + tl;
+            if (idx < nvec) st_stream(yr + (int64_t)idx * 16, X[r][i].raw);
+          }
+        }
+      } else {
+        uint32_t bits[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) bits[r] = absmax2_fold(acc[r]);
+        team_umax<R>(bits, team, bar_id, red[tm][parity][2]);
+        quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[tm][parity][3]);
+      }
+    }
+  }
+  cp_wait<0>();
+}
+
+template <typename T, int OP, int NORM, int VPL, int S, int R>
+int launch(const Args& a, int team, cudaStream_t st) {
+  const int nvec = a.N / 8;
+  const size_t tab = (OP != OP_QUANT) ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
+  const size_t per_team = (size_t)S * R * nvec * 16;
+  // Up to 512 threads and ~200 KB of shared memory per CTA, one CTA per SM.
+  int teams = 512 / team;
+  if (teams > 15) teams = 15;   // named barriers 1..15
+  while (teams > 1 && tab + teams * per_team > 200 * 1024) --teams;
+  const size_t smem = tab + teams * per_team;
+  if (smem > 200 * 1024) return JO_ERR_INVALID;
+  static size_t attr = 0;
+  if (attr < smem) {
+    cudaFuncSetAttribute(staged_rows<T, OP, NORM, VPL, S, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    attr = smem;
+  }
+  const int64_t need = ((a.M + R - 1) / R + teams - 1) / teams;
+  const int64_t grid = need < sm_count() ? need : sm_count();
+  staged_rows<T, OP, NORM, VPL, S, R><<<(unsigned)grid, team * teams, smem, st>>>(a, team, teams);
+  return JO_OK;
+}
+
+}  // namespace staged
+
+// Entry used by row_ops.cu.  Returns JO_ERR_INVALID (no launch) when the shape
+// is not covered, so the caller falls back to the register kernel.
+int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, const void* gamma, const void* beta,
+                       const void* scale, const void* shift, uint8_t* q, float* s, int64_t M, int N, float eps,
+                       cudaStream_t st) {
+  using namespace staged;
+  if (dtype != JO_DTYPE_BF16 && dtype != JO_DTYPE_F16) return JO_ERR_INVALID;
+  const int nvec = N / 8;
+  if (N % 8 != 0 || nvec < 128) return JO_ERR_INVALID;
+  const int team = ((nvec + 3) / 4 + 31) / 32 * 32;   // 4 vectors per thread
+  if (team > 512) return JO_ERR_INVALID;
+  Args a{x, y, gamma, beta, scale, shift, q, s, M, N, eps};
+  constexpr int S = 2, R = 2;
+#define JO_ST(T)                                                                                          \
+  do {                                                                                                    \
+    if (op == OP_QUANT) return launch<T, OP_QUANT, JO_NORM_RMS, 4, S, R>(a, team, st);                   \
+    if (op == OP_NORM_MOD_QUANT)                                                                          \
+      return norm == JO_NORM_RMS ? launch<T, OP_NORM_MOD_QUANT, JO_NORM_RMS, 4, S, R>(a, team, st)       \
+                                 : launch<T, OP_NORM_MOD_QUANT, JO_NORM_LAYER, 4, S, R>(a, team, st);    \
+    if (op == OP_NORM_MOD)                                                                                \
+      return norm == JO_NORM_RMS ? launch<T, OP_NORM_MOD, JO_NORM_RMS, 4, S, R>(a, team, st)             \
+                                 : launch<T, OP_NORM_MOD, JO_NORM_LAYER, 4, S, R>(a, team, st);          \
+  } while (0)
+  if (dtype == JO_DTYPE_BF16) JO_ST(__nv_bfloat16);
+  else JO_ST(__half);
+#undef JO_ST
+  return JO_ERR_INVALID;
+}
+
+}  // namespace jo

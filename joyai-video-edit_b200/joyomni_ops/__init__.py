@@ -135,7 +135,7 @@ def fused_norm_scale_shift(x, gamma, beta, scale, shift, norm_type, eps=1e-5):
     _check_cuda(scale, "scale")
     _check_cuda(shift, "shift")
     _chk(x.dim() == 2, "x must be 2D [M, N]")
-    _chk(x.stride(-1) == 1, "x last dim must be contiguous")
+    _chk(x.stride(-1) == 1 or x.numel() == 0, "x last dim must be contiguous")
     M, N = x.shape
     _chk(N % 4 == 0, "N must be divisible by 4")
     _chk(scale.dim() == 2 and shift.dim() == 2, "scale/shift must be 2D [M, N]")
@@ -175,7 +175,7 @@ def rmsnorm(x, weight, eps=1e-6):
     _check_cuda(x, "x")
     _check_cuda(weight, "weight")
     _chk(x.dim() == 2, "x must be 2D [M, N]")
-    _chk(x.stride(-1) == 1, "x last dim must be contiguous")
+    _chk(x.stride(-1) == 1 or x.numel() == 0, "x last dim must be contiguous")
     _chk(weight.dim() == 1 and weight.numel() == x.size(1), "weight must be 1D [N]")
     _chk(x.dtype == weight.dtype, "x and weight dtype must match")
     if x.dtype not in _DT:

@@ -112,6 +112,25 @@ int jo_norm_modulate_quant_fp8(const void* x, const void* gamma, const void* bet
                                int64_t mod_stride, int64_t mod_group, int norm_type, float eps,
                                int dtype, void* out_q, float* out_s, void* stream);
 
+/*
+ * D[m, n] = out(fma(sa[m], sb[n] * acc[m, n], bias[n])) (or out(sa[m] * (sb[n] * acc))
+ * without bias), acc = sum_k A[m, k] * B[k, n] over e4m3 codes in fp32 on the
+ * tcgen05 tensor cores; epilogue JO_EPI_GELU_TANH applies GELU-tanh to the
+ * rounded result.  Replaces joyomni_ops::fp8_scaled_mm
+ *   (deploy/joyomni_ops/csrc/fp8_gemm.cu:1450-1548; epilogue :833-860).
+ * mat_a: e4m3 [M, K] row-major; mat_b: e4m3 column-major [K, N] (N rows of K
+ * codes); scales_a fp32 [M]; scales_b fp32 [N]; bias NULL or [N] of out_dtype;
+ * out [M, N] row-major, out_dtype JO_DTYPE_BF16/F16.  K % 16 == 0, N % 8 == 0,
+ * operands 16-byte aligned.
+ */
+int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                     const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
+                     void* stream);
+
+/* Diagnostic: fault code left by a GEMM wait that timed out (0 = none);
+ * reset != 0 clears it.  Synchronous; for tests. */
+int jo_gemm_last_fault(int reset);
+
 #ifdef __cplusplus
 }
 #endif

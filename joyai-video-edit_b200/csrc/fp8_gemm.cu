@@ -1,0 +1,477 @@
+// FP8 (e4m3 x e4m3 -> fp32) scaled GEMM for sm_100a on the 5th-generation
+// tensor cores (tcgen05 + TMEM), with the per-token x per-channel scale, bias
+// and optional GELU-tanh epilogue fused.
+//
+// Replaces joyomni_ops::fp8_scaled_mm (deploy/joyomni_ops/csrc/fp8_gemm.cu:1450-1548,
+// Sm100 CUTLASS kernel :796-1170).  Epilogue arithmetic follows that kernel's
+// visitor tree (:833-860): t = sb[n] * acc (fp32), D = out(fma(sa[m], t, bias[n]))
+// or out(sa[m] * t) without bias.  The GELU variant applies
+// 0.5*y*(1+tanh(sqrt(2/pi)*(y+0.044715*y^3))) to the rounded D, as the reference
+// model applies F.gelu(approximate="tanh") after fp8_scaled_mm (dit.py:90-92).
+//
+// Layout: A [M, K] row-major (K contiguous); B given as the column-major [K, N]
+// operand of the reference, i.e. N rows of K contiguous codes.  Both operands
+// are therefore K-major, loaded by TMA with 128-byte swizzle into the canonical
+// UMMA K-major SW128 layout.  No cluster multicast anywhere: every CTA loads its
+// own tiles; operand reuse across CTAs comes from L2 via a grouped tile order.
+//
+// Kernel organisation (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: K-blocks of 128 bytes for A (128 rows) and B (256 rows)
+//               into a ring of STAGES shared-memory stages (full/empty mbarriers)
+//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (K = 32)
+//               per stage into one of two 128 x 256 fp32 accumulators in TMEM
+//               (512 columns), tcgen05.commit releases the stage / publishes the tile
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, scales + bias (+ GELU),
+//               bf16/fp16 stores; the accumulator is handed back so the MMA of the
+//               next tile overlaps this epilogue.
+// Every mbarrier wait is bounded by a clock-based timeout; on expiry the CTA sets
+// an abort flag, records an error code readable with jo_gemm_last_fault(), waits
+// (bounded) for its own in-flight copies, frees its TMEM and returns.
+#include <cuda.h>
+
+#include "jo_common.cuh"
+
+namespace jo {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes = fp8 elements per K-block
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK;              // 16 KB
+constexpr int B_STAGE = BN * BK;              // 32 KB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+__device__ int g_fault = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false (and raises the CTA abort flag) on timeout or
+// when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      atomicCAS(&g_fault, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);          // start address
+  d |= (uint64_t)1 << 16;                           // leading byte offset (unused for SW128 K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;                 // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                           // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f8f6f4, A = B = E4M3, D = F32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc(int m, int n) {
+  return (1u << 4)                      // D format F32
+         | (0u << 7) | (0u << 10)       // A, B = E4M3
+         | ((uint32_t)(n >> 3) << 17)   // N / 8
+         | ((uint32_t)(m >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(accum));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float gelu_tanh(float y) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float u = k0 * (y + 0.044715f * y * y * y);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * y * (1.f + t);
+}
+
+struct Params {
+  void* d;
+  const float* sa;
+  const float* sb;
+  const void* bias;
+  int M, N, K;
+  int m_blocks, n_blocks, k_blocks;
+  int epilogue;  // JO_EPI_*
+};
+
+// Grouped rasterisation: GROUP m-blocks share the n sweep, keeping the live
+// A and B panels of all 148 CTAs inside L2.
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
+  constexpr int GROUP = 16;
+  const int per_group = GROUP * p.n_blocks;
+  const int g = t / per_group;
+  const int first = g * GROUP;
+  const int rows = min(GROUP, p.m_blocks - first);
+  const int r = t % per_group;
+  mb = first + r % rows;
+  nb = r / rows;
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(THREADS, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars: full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES);
+  const uint32_t tempty0 = smem_u32(bars + 2 * STAGES + 2);
+  const int num_tiles = p.m_blocks * p.n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, 1)) { ok = false; break; }
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          mbar_expect_tx(full0 + 8 * s, STAGE_BYTES);
+          tma_load_2d(sa, &tmap_a, kb * BK, mb * BM, full0 + 8 * s);
+          tma_load_2d(sa + A_STAGE, &tmap_b, kb * BK, nb * BN, full0 + 8 * s);
+        }
+      }
+      // Drain: every copy this thread issued must have landed before the CTA exits.
+      const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
+      for (uint32_t j = it - n; j < it; ++j) {
+        const int s = j % STAGES;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(full0 + 8 * s, (j / STAGES) & 1) && clock64() - t0 < kTimeoutCycles) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      constexpr uint32_t ID = idesc(BM, BN);
+      uint32_t it = 0;
+      int tc = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tc) {
+        const int buf = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        if (!mbar_wait(tempty0 + 8 * buf, tph ^ 1, abort_flag, 2)) break;
+        fence_after();
+        const uint32_t dtm = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, 3)) { ok = false; break; }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_STAGE;
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            mma_f8(dtm, sdesc(sa + 32 * k), sdesc(sb + 32 * k), ID, (kb | k) != 0);
+          }
+          mma_commit(empty0 + 8 * s);   // stage free once these MMAs have read it
+        }
+        if (ok) mma_commit(tfull0 + 8 * buf);  // accumulator ready for the epilogue
+      }
+      // Drain outstanding MMAs before TMEM is released.
+      if (it > 0) {
+        const uint32_t j = it - 1;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(empty0 + 8 * (j % STAGES), (j / STAGES) & 1) && clock64() - t0 < kTimeoutCycles) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue --
+    const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int tc = 0;
+    OutT* D = static_cast<OutT*>(p.d);
+    const OutT* bias = static_cast<const OutT*>(p.bias);
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const int buf = tc & 1;
+      const uint32_t tph = (tc >> 1) & 1;
+      if (!mbar_wait(tfull0 + 8 * buf, tph, abort_flag, 4)) break;
+      fence_after();
+      const int m = mb * BM + row_in_tile;
+      const bool mok = m < p.M;
+      const float sa = mok ? __ldg(p.sa + m) : 0.f;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      OutT* drow = D + (size_t)(mok ? m : 0) * p.N;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(tbase + c, r);
+        tmem_wait_ld();
+        const int n0 = nb * BN + c;
+        if (!mok || n0 >= p.N) continue;
+        float y[32];
+        const bool full = n0 + 32 <= p.N;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float sbv[4], bv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (full) {
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
+            sbv[0] = s4.x; sbv[1] = s4.y; sbv[2] = s4.z; sbv[3] = s4.w;
+            if (bias) {
+              const uint2 b2 = __ldg(reinterpret_cast<const uint2*>(bias + n0 + j));
+              const OutT* bb = reinterpret_cast<const OutT*>(&b2);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) bv[e] = to_f32(bb[e]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int n = n0 + j + e;
+              sbv[e] = n < p.N ? p.sb[n] : 0.f;
+              if (bias) bv[e] = n < p.N ? to_f32(bias[n]) : 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float acc = __uint_as_float(r[j + e]);
+            const float tt = __fmul_rn(sbv[e], acc);
+            float o = bias ? __fmaf_rn(sa, tt, bv[e]) : __fmul_rn(sa, tt);
+            if (p.epilogue == JO_EPI_GELU_TANH) o = gelu_tanh(to_f32(from_f32<OutT>(o)));
+            y[j + e] = o;
+          }
+        }
+        if (full) {
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = pack2<OutT>(y[2 * j], y[2 * j + 1]);
+          uint4* dst = reinterpret_cast<uint4*>(drow + n0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) drow[n0 + j] = from_f32<OutT>(y[j]);
+        }
+      }
+      // hand the accumulator back to the MMA warp
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------- host --
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// 2-D K-major map over `rows` rows of `k` bytes with a box of box_rows x 128 B.
+static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename OutT>
+int launch(const void* A, const void* B, const float* sa, const float* sb, const void* bias, void* D, int64_t M,
+           int64_t N, int64_t K, int epi, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, A, M, K, BM) || !make_map(&tb, B, N, K, BN)) {
+    set_error("fp8_scaled_mm: cuTensorMapEncodeTiled failed (pointer %p/%p, M %lld N %lld K %lld)", A, B,
+              (long long)M, (long long)N, (long long)K);
+    return JO_ERR_CUDA;
+  }
+  Params p;
+  p.d = D;
+  p.sa = sa;
+  p.sb = sb;
+  p.bias = bias;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.m_blocks = (int)((M + BM - 1) / BM);
+  p.n_blocks = (int)((N + BN - 1) / BN);
+  p.k_blocks = (int)((K + BK - 1) / BK);
+  p.epilogue = epi;
+  const int smem = STAGES * STAGE_BYTES + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(fp8_gemm_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  const int tiles = p.m_blocks * p.n_blocks;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  fp8_gemm_kernel<OutT><<<grid, THREADS, smem, st>>>(ta, tb, p);
+  return check_launch("fp8_scaled_mm");
+}
+
+}  // namespace gemm
+}  // namespace jo
+
+extern "C" {
+
+int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                     const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
+                     void* stream) {
+  using namespace jo;
+  const char* what = "fp8_scaled_mm";
+  JO_REQUIRE(out_dtype == JO_DTYPE_BF16 || out_dtype == JO_DTYPE_F16, JO_ERR_DTYPE,
+             "out_dtype must be Half or BFloat16");
+  JO_REQUIRE(epilogue == JO_EPI_NONE || epilogue == JO_EPI_GELU_TANH, JO_ERR_INVALID, "%s: unknown epilogue %d",
+             what, epilogue);
+  JO_REQUIRE(M >= 0 && N >= 0 && K >= 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), JO_ERR_INVALID,
+             "%s: invalid shape", what);
+  JO_REQUIRE(K % 16 == 0, JO_ERR_INVALID, "mat_a must be multiple of 16 bytes for memory alignment");
+  JO_REQUIRE((N * 2) % 16 == 0, JO_ERR_INVALID, "out must be multiple of 16 bytes for memory alignment");
+  JO_REQUIRE(M == 0 || N == 0 || (mat_a && mat_b && scales_a && scales_b && out), JO_ERR_INVALID,
+             "%s: null tensor pointer", what);
+  JO_REQUIRE(aligned16(mat_a) && aligned16(mat_b) && aligned16(out) && aligned16(scales_b) &&
+                 (!bias || aligned8(bias)),
+             JO_ERR_ALIGN, "%s: operands must be 16-byte aligned (bias 8-byte)", what);
+  int st = require_sm100();
+  if (st != JO_OK) return st;
+  if (M == 0 || N == 0) return JO_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  JO_REQUIRE(K > 0, JO_ERR_INVALID, "%s: K must be positive", what);
+  return out_dtype == JO_DTYPE_BF16
+             ? gemm::launch<__nv_bfloat16>(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, epilogue, s)
+             : gemm::launch<__half>(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, epilogue, s);
+}
+
+// Fault code of the GEMM kernel's bounded waits (0 = none) and reset.  Reads
+// a device symbol synchronously; intended for tests and diagnostics only.
+int jo_gemm_last_fault(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, jo::gemm::g_fault, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return JO_ERR_CUDA;
+  }
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(jo::gemm::g_fault, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // extern "C"

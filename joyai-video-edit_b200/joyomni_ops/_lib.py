@@ -52,6 +52,7 @@ SIGNATURES = {
     "jo_per_token_quant_fp8": [_p, _i32, _p, _p, _i64, _i64, _p],
     "jo_norm_modulate_quant_fp8": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _p, _p, _p],
     "jo_fp8_scaled_mm": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
+    "jo_gemm_last_fault": [_i32],
 }
 
 for _name, _args in SIGNATURES.items():

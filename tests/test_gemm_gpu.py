@@ -1,0 +1,105 @@
+"""GPU parity of the tcgen05 FP8 scaled GEMM (jo_fp8_scaled_mm) against the CPU
+oracle's exact-dequantisation product: relative RMS <= 1e-3 and <= 2 output ulps
+per element (bf16 / fp16), over ragged M, N tails, K tails, with and without
+bias, and the fused GELU-tanh epilogue; full BASELINE shapes are checked on a
+row sample."""
+import numpy as np
+import pytest
+import torch
+
+import joyomni_oracle as O
+from _util import assert_close_ulp, randn
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def jo(cuda):
+    import joyomni_ops
+    if not joyomni_ops.has_fp8():
+        pytest.skip("GEMM not built")
+    return joyomni_ops
+
+
+def _operands(rng, M, N, K):
+    a, sa = O.per_token_quant_fp8(randn(rng, (M, K)))
+    b, sb = O.quantize_weight_per_channel(randn(rng, (N, K), 0.02))
+    return a, sa, b, sb
+
+
+def _run(jo, dev, a, sa, b, sb, bias, out_dtype=torch.bfloat16, gelu=False):
+    A = torch.from_numpy(a).to(dev).view(torch.float8_e4m3fn)
+    B = torch.from_numpy(b).to(dev).view(torch.float8_e4m3fn).t()
+    bt = None if bias is None else torch.from_numpy(bias).to(out_dtype).to(dev)
+    f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
+    return f(A, B, torch.from_numpy(sa).to(dev), torch.from_numpy(sb).to(dev), out_dtype, bt)
+
+
+SHAPES = [(1, 64, 128), (5, 256, 32), (128, 256, 128), (130, 384, 256), (300, 256, 512), (257, 520, 1008),
+          (1000, 768, 640), (64, 16, 48), (513, 1024, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_fp8_scaled_mm_vs_oracle(jo, cuda, M, N, K, with_bias):
+    rng = np.random.default_rng(M * 31 + N * 7 + K)
+    a, sa, b, sb = _operands(rng, M, N, K)
+    bias = randn(rng, (N,), 0.01) if with_bias else None
+    y = _run(jo, cuda, a, sa, b, sb, bias)
+    ref = O.fp8_scaled_mm(a, b, sa, sb, bias)
+    assert_close_ulp(y.float().cpu().numpy(), ref, max_ulp=2, rel_rms=1e-3)
+    assert jo._lib.lib.jo_gemm_last_fault(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 512, 256), (77, 264, 128)])
+def test_fp8_scaled_mm_gelu(jo, cuda, M, N, K):
+    rng = np.random.default_rng(5)
+    a, sa, b, sb = _operands(rng, M, N, K)
+    # larger activations so GELU's non-linear range is exercised
+    sa = (sa * 40).astype(np.float32)
+    bias = randn(rng, (N,), 0.5)
+    y = _run(jo, cuda, a, sa, b, sb, bias, gelu=True)
+    ref = O.fp8_scaled_mm(a, b, sa, sb, bias, epilogue="gelu_tanh")
+    assert_close_ulp(y.float().cpu().numpy(), ref, max_ulp=2, rel_rms=2e-3, atol=1e-4)
+
+
+def test_fp8_scaled_mm_fp16_out(jo, cuda):
+    rng = np.random.default_rng(6)
+    a, sa, b, sb = _operands(rng, 150, 256, 384)
+    bias = randn(rng, (256,), 0.01)
+    y = _run(jo, cuda, a, sa, b, sb, bias, out_dtype=torch.float16)
+    ref = O.fp8_scaled_mm(a, b, sa, sb, O.round_f16(bias), out="f16")
+    assert_close_ulp(y.float().cpu().numpy(), ref, dtype="f16", max_ulp=2, rel_rms=1e-3)
+
+
+def test_fp8_scaled_mm_rejects_bad_inputs(jo, cuda):
+    A = torch.zeros(8, 32, device=cuda).to(torch.float8_e4m3fn)
+    B = torch.zeros(64, 32, device=cuda).to(torch.float8_e4m3fn).t()
+    s8, s64 = torch.ones(8, device=cuda), torch.ones(64, device=cuda)
+    with pytest.raises(RuntimeError, match="column major"):
+        jo.fp8_scaled_mm(A, B.contiguous(), s8, s64, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="out_dtype"):
+        jo.fp8_scaled_mm(A, B, s8, s64, torch.float32)
+    with pytest.raises(RuntimeError, match="bias dtype"):
+        jo.fp8_scaled_mm(A, B, s8, s64, torch.bfloat16, torch.ones(64, device=cuda))
+    with pytest.raises(RuntimeError, match="scales_a"):
+        jo.fp8_scaled_mm(A, B, s64, s64, torch.bfloat16)
+
+
+@pytest.mark.parametrize("N,gelu", [(15360, False), (13824, True)])
+def test_fp8_scaled_mm_full_size_row_sample(jo, cuda, N, gelu):
+    """BASELINE config 3 shapes (M = 10530, K = 5120): every row is computed by the
+    kernel; a seeded sample of rows (including the ragged last M-tile) is checked
+    against the oracle."""
+    M, K = 10530, 5120
+    g = torch.Generator(device="cpu").manual_seed(3)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    a, sa = O.per_token_quant_fp8(x.float().numpy())
+    w = (0.02 * torch.randn(N, K, generator=g)).to(torch.bfloat16).float().numpy()
+    b, sb = O.quantize_weight_per_channel(w)
+    bias = O.round_bf16(0.01 * np.random.default_rng(1).standard_normal(N).astype(np.float32))
+    y = _run(jo, cuda, a, sa, b, sb, bias, gelu=gelu).float().cpu().numpy()
+    rows = np.unique(np.concatenate([np.random.default_rng(2).integers(0, M, 24), [0, 127, 128, M - 35, M - 1]]))
+    ref = O.fp8_scaled_mm(a[rows], b, sa[rows], sb, bias, epilogue="gelu_tanh" if gelu else "none")
+    assert_close_ulp(y[rows], ref, max_ulp=2, rel_rms=2e-3 if gelu else 1e-3, atol=1e-4 if gelu else 1e-6)
+    assert np.isfinite(y).all()

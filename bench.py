@@ -352,7 +352,9 @@ def kernel_table(torch, jo, dev):
 
 
 def gemm_table(torch, jo, dev, gen):
-    pk = peaks()
+    """M = 10530, K = 5120; N = 15360 (QKV, + bias) and
+    N = 13824 (FFN up, + bias + fused GELU-tanh).  Dense FP8 roofline: the
+    nominal 4.5 PFLOP/s (no measured FP8 peak exists on this pool)."""
     out = {}
     M, K = M_CFG2, N_CFG2
     a = torch.randn(M, K, generator=gen).to(torch.bfloat16).to(dev)
@@ -360,20 +362,16 @@ def gemm_table(torch, jo, dev, gen):
     sa = torch.empty(M, dtype=torch.float32, device=dev)
     jo.sgl_per_token_quant_fp8(a, aq, sa)
     for name, N, gelu in (("cfg3a_fp8_gemm_qkv_bias", 15360, False), ("cfg3b_fp8_gemm_ffn_up_bias_gelu", 13824, True)):
-        wq = torch.randint(-100, 100, (N, K), generator=gen, dtype=torch.int8).view(torch.uint8)
-        wq = (wq & 0x7F | (wq & 0x80)).view(torch.float8_e4m3fn)
-        wq = torch.where(torch.isnan(wq.float()), torch.zeros_like(wq.float()), wq.float()).to(torch.float8_e4m3fn)
-        b = wq.to(dev).t()
+        wq = (torch.randn(N, K, generator=gen) * 30).clamp(-448, 448).to(torch.float8_e4m3fn).to(dev).t()
         sb = (torch.rand(N, generator=gen) * 1e-3).to(dev)
         bias = (0.01 * torch.randn(N, generator=gen)).to(torch.bfloat16).to(dev)
         f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
-        fns = [lambda: f(aq, b, sa, sb, torch.bfloat16, bias) for _ in range(5)]
-        ms, _ = graph_time(torch, fns, 5)
+        ms, _ = graph_time(torch, [lambda: f(aq, wq, sa, sb, torch.bfloat16, bias) for _ in range(5)], 5)
         fl = 2.0 * M * N * K
         t = ms / 5 * 1e-3
-        out[name] = {"us": round(ms / 5 * 1e3, 2), "tflops": round(fl / t / 1e12, 1),
-                     "frac_of_dense_fp8_nominal_4500": round(fl / t / 4.5e15, 4),
-                     "frac_of_measured_bf16_x2": round(fl / t / (2 * pk["bf16_tflops"] * 1e12), 4)}
+        out[name] = {"us": round(ms / 5 * 1e3, 1), "tflops": round(fl / t / 1e12, 1),
+                     "frac_of_dense_fp8_nominal_4500": round(fl / t / 4.5e15, 4)}
+        del wq
     return out
 
 

@@ -28,6 +28,7 @@
 // an abort flag, records an error code readable with jo_gemm_last_fault(), waits
 // (bounded) for its own in-flight copies, frees its TMEM and returns.
 #include <cuda.h>
+#include <stdlib.h>
 
 #include "jo_common.cuh"
 
@@ -361,6 +362,296 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------------------- 2-SM variant --
+// A CTA pair (cluster of 2) computes a 256 x 256 tile with tcgen05.mma
+// cta_group::2: CTA r holds A rows [r*128, r*128+128) and B rows (N) of the same
+// half in its own shared memory at identical offsets; the even CTA issues the
+// MMAs, which read both CTAs' operands and write each CTA's 128 accumulator
+// rows into that CTA's TMEM.  Per CTA and K-block only 32 KB cross L2 (16 KB of
+// A + 16 KB of B) for 128 x 256 outputs, against 48 KB in the 1-SM kernel, and
+// the ring is 6 stages deep.  Loads are plain per-CTA TMA loads (no multicast);
+// their completion is counted on the even CTA's barrier (.cta_group::2).
+constexpr int STAGES2 = 6;
+constexpr int A2_STAGE = 128 * BK;   // 16 KB: this CTA's 128 rows of A
+constexpr int B2_STAGE = 128 * BK;   // 16 KB: this CTA's 128 rows of B
+constexpr int STAGE2_BYTES = A2_STAGE + B2_STAGE;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx_cluster(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      atomicCAS(&g_fault, 0, code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(leader_bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f8_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(accum));
+}
+// Arrive (once all prior MMAs of this thread complete) on the barrier at the
+// same shared-memory offset in both CTAs of the pair.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .b16 m;\n mov.b16 m, 3;\n"
+      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}\n" ::"r"(
+          bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tile_coords2(int t, int m_blocks, int n_blocks, int& mb, int& nb) {
+  constexpr int GROUP = 8;
+  const int per_group = GROUP * n_blocks;
+  const int g = t / per_group;
+  const int first = g * GROUP;
+  const int rows = min(GROUP, m_blocks - first);
+  const int r = t % per_group;
+  mb = first + r % rows;
+  nb = r / rows;
+}
+
+template <typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    fp8_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + STAGES2);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES2);
+  const uint32_t tempty0 = smem_u32(bars + 2 * STAGES2 + 2);
+  // p.m_blocks counts 256-row pair tiles here
+  const int num_tiles = p.m_blocks * p.n_blocks;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(full0 + 8 * s, 1);    // leader only uses it: 1 expect_tx arrival + both CTAs' bytes
+      mbar_init(empty0 + 8 * s, 1);   // one multicast commit per use
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);   // one multicast commit per tile
+      mbar_init(tempty0 + 8 * b, 8);  // leader only: 4 epilogue warps x 2 CTAs
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  cluster_sync();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+      const uint32_t lfull0 = map_to_rank(full0, 0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        int mb, nb;
+        tile_coords2(t, p.m_blocks, p.n_blocks, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, 11)) { ok = false; break; }
+          const uint32_t sa = smem_u32(smem + s * STAGE2_BYTES);
+          if (leader) mbar_expect_tx_cluster(full0 + 8 * s, 2 * STAGE2_BYTES);
+          tma_load_2d_pair(sa, &tmap_a, kb * BK, mb * 256 + rank * 128, lfull0 + 8 * s);
+          tma_load_2d_pair(sa + A2_STAGE, &tmap_b, kb * BK, nb * BN + rank * 128, lfull0 + 8 * s);
+        }
+      }
+      // Drain: the last use of each stage must be consumed (its empty phase completes)
+      // before this CTA may exit, so no copy of ours is still in flight.
+      const uint32_t n = it < (uint32_t)STAGES2 ? it : (uint32_t)STAGES2;
+      for (uint32_t j = it - n; j < it; ++j) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(empty0 + 8 * (j % STAGES2), (j / STAGES2) & 1) && clock64() - t0 < kTimeoutCycles) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------- MMA issuer (even CTA) --
+    if (leader && lane == 0) {
+      constexpr uint32_t ID = idesc(256, BN);
+      uint32_t it = 0;
+      int tc = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++tc) {
+        const int buf = tc & 1;
+        const uint32_t tph = (tc >> 1) & 1;
+        if (!mbar_wait_cluster(tempty0 + 8 * buf, tph ^ 1, abort_flag, 12)) break;
+        fence_after();
+        const uint32_t dtm = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1;
+          if (!mbar_wait_cluster(full0 + 8 * s, ph, abort_flag, 13)) { ok = false; break; }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE2_BYTES);
+          const uint32_t sb = sa + A2_STAGE;
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_f8_pair(dtm, sdesc(sa + 32 * k), sdesc(sb + 32 * k), ID, (kb | k) != 0);
+          mma_commit_pair(empty0 + 8 * s);
+        }
+        if (ok) mma_commit_pair(tfull0 + 8 * buf);
+      }
+      if (it > 0) {
+        const uint32_t j = it - 1;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(empty0 + 8 * (j % STAGES2), (j / STAGES2) & 1) && clock64() - t0 < kTimeoutCycles) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue --
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t ltempty0 = map_to_rank(tempty0, 0);
+    int tc = 0;
+    OutT* D = static_cast<OutT*>(p.d);
+    const OutT* bias = static_cast<const OutT*>(p.bias);
+    for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+      int mb, nb;
+      tile_coords2(t, p.m_blocks, p.n_blocks, mb, nb);
+      const int buf = tc & 1;
+      const uint32_t tph = (tc >> 1) & 1;
+      if (!mbar_wait_cluster(tfull0 + 8 * buf, tph, abort_flag, 14)) break;
+      fence_after();
+      const int m = mb * 256 + (int)rank * 128 + row_in_tile;
+      const bool mok = m < p.M;
+      const float sa = mok ? __ldg(p.sa + m) : 0.f;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      OutT* drow = D + (size_t)(mok ? m : 0) * p.N;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(tbase + c, r);
+        tmem_wait_ld();
+        const int n0 = nb * BN + c;
+        if (!mok || n0 >= p.N) continue;
+        float y[32];
+        const bool full = n0 + 32 <= p.N;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float sbv[4], bv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (full) {
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
+            sbv[0] = s4.x; sbv[1] = s4.y; sbv[2] = s4.z; sbv[3] = s4.w;
+            if (bias) {
+              const uint2 b2 = __ldg(reinterpret_cast<const uint2*>(bias + n0 + j));
+              const OutT* bb = reinterpret_cast<const OutT*>(&b2);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) bv[e] = to_f32(bb[e]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int n = n0 + j + e;
+              sbv[e] = n < p.N ? p.sb[n] : 0.f;
+              if (bias) bv[e] = n < p.N ? to_f32(bias[n]) : 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float acc = __uint_as_float(r[j + e]);
+            const float tt = __fmul_rn(sbv[e], acc);
+            float o = bias ? __fmaf_rn(sa, tt, bv[e]) : __fmul_rn(sa, tt);
+            if (p.epilogue == JO_EPI_GELU_TANH) o = gelu_tanh(to_f32(from_f32<OutT>(o)));
+            y[j + e] = o;
+          }
+        }
+        if (full) {
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = pack2<OutT>(y[2 * j], y[2 * j + 1]);
+          uint4* dst = reinterpret_cast<uint4*>(drow + n0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) drow[n0 + j] = from_f32<OutT>(y[j]);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(ltempty0 + 8 * buf);
+    }
+  }
+
+  fence_before();
+  cluster_sync();
+  fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // ------------------------------------------------------------------- host --
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -393,11 +684,57 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// JOYOMNI_GEMM_2SM=0 selects the 1-SM kernel for every shape (A/B testing).
+static bool use_2sm() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("JOYOMNI_GEMM_2SM");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <typename OutT>
+int launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, Params p, cudaStream_t st) {
+  const int smem = STAGES2 * STAGE2_BYTES + 1024 + 256;
+  static bool attr = false;
+  static int max_pairs = 0;
+  if (!attr) {
+    cudaFuncSetAttribute(fp8_gemm_2sm_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(2 * 74);
+    q.blockDim = dim3(THREADS);
+    q.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    q.attrs = at;
+    q.numAttrs = 1;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, fp8_gemm_2sm_kernel<OutT>, &q) != cudaSuccess || nc <= 0) {
+      cudaGetLastError();
+      nc = sm_count() / 2;
+    }
+    max_pairs = nc;
+    attr = true;
+  }
+  p.m_blocks = (p.M + 255) / 256;
+  const int tiles = p.m_blocks * p.n_blocks;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  if (getenv("JOYOMNI_GEMM_DEBUG"))
+    fprintf(stderr, "[jo gemm 2sm] max_pairs %d tiles %d grid %d smem %d\n", max_pairs, tiles, 2 * pairs, smem);
+  fp8_gemm_2sm_kernel<OutT><<<2 * pairs, THREADS, smem, st>>>(ta, tb, p);
+  return check_launch("fp8_scaled_mm");
+}
+
 template <typename OutT>
 int launch(const void* A, const void* B, const float* sa, const float* sb, const void* bias, void* D, int64_t M,
            int64_t N, int64_t K, int epi, cudaStream_t st) {
   CUtensorMap ta, tb;
-  if (!make_map(&ta, A, M, K, BM) || !make_map(&tb, B, N, K, BN)) {
+  const bool pair = M > 128 && use_2sm();
+  if (!make_map(&ta, A, M, K, BM) || !make_map(&tb, B, N, K, pair ? 128 : BN)) {
     set_error("fp8_scaled_mm: cuTensorMapEncodeTiled failed (pointer %p/%p, M %lld N %lld K %lld)", A, B,
               (long long)M, (long long)N, (long long)K);
     return JO_ERR_CUDA;
@@ -414,6 +751,7 @@ int launch(const void* A, const void* B, const float* sa, const float* sb, const
   p.n_blocks = (int)((N + BN - 1) / BN);
   p.k_blocks = (int)((K + BK - 1) / BK);
   p.epilogue = epi;
+  if (pair) return launch_2sm<OutT>(ta, tb, p, st);
   const int smem = STAGES * STAGE_BYTES + 1024 + 256;
   static bool attr = false;
   if (!attr) {

@@ -366,11 +366,22 @@ def gemm_table(torch, jo, dev, gen):
         sb = (torch.rand(N, generator=gen) * 1e-3).to(dev)
         bias = (0.01 * torch.randn(N, generator=gen)).to(torch.bfloat16).to(dev)
         f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
-        ms, _ = graph_time(torch, [lambda: f(aq, wq, sa, sb, torch.bfloat16, bias) for _ in range(5)], 5)
+        ms, g = graph_time(torch, [lambda: f(aq, wq, sa, sb, torch.bfloat16, bias) for _ in range(5)], 5)
+        # clocks under a sustained GEMM load (~1 s of back-to-back replays)
+        clk = ClockSampler(dev.index or 0)
+        clk.start()
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            g.replay()
+            torch.cuda.synchronize()
+        ck = clk.stop()
         fl = 2.0 * M * N * K
         t = ms / 5 * 1e-3
+        pk = peaks()
         out[name] = {"us": round(ms / 5 * 1e3, 1), "tflops": round(fl / t / 1e12, 1),
-                     "frac_of_dense_fp8_nominal_4500": round(fl / t / 4.5e15, 4)}
+                     "frac_of_dense_fp8_nominal_4500": round(fl / t / 4.5e15, 4),
+                     "frac_of_2x_measured_bf16_burst": round(fl / t / (2e12 * pk["bf16_tflops"]), 4),
+                     "clocks_sustained": ck}
         del wq
     return out
 

@@ -65,6 +65,18 @@ int jo_fused_qk_norm_rope_3d_paired(void* q, void* k, int64_t batch, int64_t seq
                                     const void* cos, const void* sin, void* stream);
 
 /*
+ * Strided form of jo_fused_qk_norm_rope_3d_paired (no reference counterpart):
+ * q and k are [batch*seq_len, num_heads, head_dim] bf16 views whose tokens are
+ * q_token_stride / k_token_stride elements apart (e.g. the q and k thirds of a
+ * fused QKV GEMM output), processed in place with the same arithmetic.  With
+ * cos = sin = NULL only the per-head RMSNorm is applied.  Strides % 8 == 0.
+ */
+int jo_qk_norm_rope_strided(void* q, void* k, int64_t batch, int64_t seq_len, int64_t num_heads,
+                            int64_t head_dim, int64_t q_token_stride, int64_t k_token_stride, float eps,
+                            const void* q_weight, const void* k_weight, const void* cos, const void* sin,
+                            void* stream);
+
+/*
  * y = Norm(x; gamma, beta) * (1 + scale) + shift, norm_type JO_NORM_LAYER/RMS.
  * Replaces joyomni_ops::fused_norm_scale_shift
  *   (deploy/joyomni_ops/csrc/fused_norm_scale_shift.cu:172-209).

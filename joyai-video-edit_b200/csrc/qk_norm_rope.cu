@@ -23,11 +23,13 @@
 namespace jo {
 namespace {
 
-template <int D, int U>
+// q_ts / k_ts: elements between consecutive tokens (num_heads * D when dense);
+// heads of a token are D elements apart.  ROPE = false normalises only.
+template <int D, int U, bool ROPE>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t slots, int seq_len, int num_heads,
     float eps, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
-    const __nv_bfloat16* __restrict__ cosp, const __nv_bfloat16* __restrict__ sinp) {
+    const __nv_bfloat16* __restrict__ cosp, const __nv_bfloat16* __restrict__ sinp, int64_t q_ts, int64_t k_ts) {
   constexpr int LPH = D / 8;        // lanes per head vector
   constexpr int HPW = 32 / LPH;     // head slots per warp per group
   constexpr int P = 256 / D;        // reference lanes folded into one lane
@@ -41,13 +43,17 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   wk.raw = ld_cached(kw + hl * 8);
 
   Vec16<__nv_bfloat16> vq[U], vk[U];
-  int64_t slot[U];
+  int64_t slot[U], qo[U], ko[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     slot[u] = (warp * U + u) * HPW + lane / LPH;
+    const int64_t tok = slot[u] / num_heads;          // (batch, token) row
+    const int64_t head = slot[u] - tok * num_heads;
+    qo[u] = tok * q_ts + head * D + hl * 8;
+    ko[u] = tok * k_ts + head * D + hl * 8;
     if (slot[u] < slots) {
-      vq[u].raw = ld_stream(q + slot[u] * D + hl * 8);
-      vk[u].raw = ld_stream(k + slot[u] * D + hl * 8);
+      vq[u].raw = ld_stream(q + qo[u]);
+      vk[u].raw = ld_stream(k + ko[u]);
     }
   }
 
@@ -56,8 +62,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const bool ok = slot[u] < slots;
     const int64_t token = ok ? (slot[u] / num_heads) % seq_len : 0;
     // cos/sin entries for this lane's 4 pairs: indices hl*4 .. hl*4+3.
-    uint2 c2 = __ldg(reinterpret_cast<const uint2*>(cosp + token * (D / 2) + hl * 4));
-    uint2 s2 = __ldg(reinterpret_cast<const uint2*>(sinp + token * (D / 2) + hl * 4));
+    uint2 c2 = make_uint2(0, 0), s2 = make_uint2(0, 0);
+    if (ROPE) {
+      c2 = __ldg(reinterpret_cast<const uint2*>(cosp + token * (D / 2) + hl * 4));
+      s2 = __ldg(reinterpret_cast<const uint2*>(sinp + token * (D / 2) + hl * 4));
+    }
     const __nv_bfloat16* cv = reinterpret_cast<const __nv_bfloat16*>(&c2);
     const __nv_bfloat16* sv = reinterpret_cast<const __nv_bfloat16*>(&s2);
 #pragma unroll
@@ -89,6 +98,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
       const float rms_rcp = rsqrtf(part[0] / static_cast<float>(D) + eps);
 #pragma unroll
       for (int j = 0; j < 8; ++j) e[j] *= rms_rcp * w.get(j);
+      if (!ROPE) {
+#pragma unroll
+        for (int j = 0; j < 8; j += 2)
+          reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(e[j], e[j + 1]));
+        continue;
+      }
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         const float c = __bfloat162float(cv[j / 2]);
@@ -101,23 +116,31 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
       }
     }
     if (ok) {
-      st_stream(q + slot[u] * D + hl * 8, vq[u].raw);
-      st_stream(k + slot[u] * D + hl * 8, vk[u].raw);
+      st_stream(q + qo[u], vq[u].raw);
+      st_stream(k + ko[u], vk[u].raw);
     }
   }
 }
 
 template <int D>
 int launch(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
-           const void* c, const void* s, cudaStream_t st) {
+           const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
   constexpr int U = 2;
   constexpr int HPW = 32 / (D / 8);
   const int64_t warps = (slots + (int64_t)HPW * U - 1) / ((int64_t)HPW * U);
   const int64_t blocks = (warps + 7) / 8;
-  qk_norm_rope_kernel<D, U><<<(unsigned)blocks, 256, 0, st>>>(
-      static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), slots, seq_len, num_heads, eps,
-      static_cast<const __nv_bfloat16*>(qw), static_cast<const __nv_bfloat16*>(kw),
-      static_cast<const __nv_bfloat16*>(c), static_cast<const __nv_bfloat16*>(s));
+  auto* qp = static_cast<__nv_bfloat16*>(q);
+  auto* kp = static_cast<__nv_bfloat16*>(k);
+  auto* qwp = static_cast<const __nv_bfloat16*>(qw);
+  auto* kwp = static_cast<const __nv_bfloat16*>(kw);
+  auto* cp = static_cast<const __nv_bfloat16*>(c);
+  auto* sp = static_cast<const __nv_bfloat16*>(s);
+  if (c)
+    qk_norm_rope_kernel<D, U, true><<<(unsigned)blocks, 256, 0, st>>>(qp, kp, slots, seq_len, num_heads, eps, qwp,
+                                                                      kwp, cp, sp, q_ts, k_ts);
+  else
+    qk_norm_rope_kernel<D, U, false><<<(unsigned)blocks, 256, 0, st>>>(qp, kp, slots, seq_len, num_heads, eps, qwp,
+                                                                       kwp, cp, sp, q_ts, k_ts);
   return check_launch("fused_qk_norm_rope_3d_paired");
 }
 
@@ -145,9 +168,53 @@ extern "C" int jo_fused_qk_norm_rope_3d_paired(void* q, void* k, int64_t batch, 
   if (st != JO_OK) return st;
   if (slots == 0) return JO_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t ts = num_heads * head_dim;
   switch (head_dim) {
-    case 64: return launch<64>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, s);
-    case 128: return launch<128>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, s);
-    default: return launch<256>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, s);
+    case 64: return launch<64>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, ts, ts, s);
+    case 128:
+      return launch<128>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, ts, ts, s);
+    default:
+      return launch<256>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, ts, ts, s);
+  }
+}
+
+// Strided variant (no reference counterpart): q and k are [B*L, H, D] views
+// whose tokens are q_token_stride / k_token_stride elements apart, e.g. the q
+// and k thirds of a fused [B*L, 3, H, D] QKV GEMM output, normalised (and,
+// when cos/sin are given, rotated) in place without the reference shim's
+// .contiguous() copies (deploy/xvideo/models/dit/sgl_fused_ops.py:74-75).
+// cos = sin = NULL: per-head RMSNorm only (the text stream's q/k norm,
+// dit.py:384-385).
+extern "C" int jo_qk_norm_rope_strided(void* q, void* k, int64_t batch, int64_t seq_len, int64_t num_heads,
+                                       int64_t head_dim, int64_t q_token_stride, int64_t k_token_stride, float eps,
+                                       const void* q_weight, const void* k_weight, const void* cos, const void* sin,
+                                       void* stream) {
+  using namespace jo;
+  JO_REQUIRE(batch >= 0 && seq_len >= 0 && num_heads >= 0, JO_ERR_INVALID, "qk_norm_rope_strided: negative size");
+  JO_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, JO_ERR_INVALID,
+             "Unsupported head_dim for qk_norm_rope_strided: %lld", (long long)head_dim);
+  JO_REQUIRE(q_token_stride >= num_heads * head_dim && k_token_stride >= num_heads * head_dim &&
+                 q_token_stride % 8 == 0 && k_token_stride % 8 == 0,
+             JO_ERR_INVALID, "qk_norm_rope_strided: token strides must cover the heads and be multiples of 8");
+  JO_REQUIRE((cos == nullptr) == (sin == nullptr), JO_ERR_INVALID, "qk_norm_rope_strided: give both cos and sin or neither");
+  const int64_t slots = batch * seq_len * num_heads;
+  JO_REQUIRE(slots == 0 || (q && k && q_weight && k_weight), JO_ERR_INVALID, "qk_norm_rope_strided: null pointer");
+  JO_REQUIRE(aligned16(q) && aligned16(k) && aligned16(q_weight) && aligned16(k_weight) &&
+                 (!cos || (aligned8(cos) && aligned8(sin))),
+             JO_ERR_ALIGN, "qk_norm_rope_strided: q/k/weights must be 16-byte aligned, cos/sin 8-byte");
+  int st = require_sm100();
+  if (st != JO_OK) return st;
+  if (slots == 0) return JO_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (head_dim) {
+    case 64:
+      return launch<64>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, q_token_stride,
+                        k_token_stride, s);
+    case 128:
+      return launch<128>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, q_token_stride,
+                         k_token_stride, s);
+    default:
+      return launch<256>(q, k, slots, (int)seq_len, (int)num_heads, eps, q_weight, k_weight, cos, sin, q_token_stride,
+                         k_token_stride, s);
   }
 }

@@ -33,6 +33,7 @@ __all__ = [
     "has_fp8",
     "norm_modulate_quant_fp8",
     "fp8_scaled_mm_gelu",
+    "qk_norm_rope_strided",
 ]
 
 _DT = {torch.float32: _lib.JO_DTYPE_F32, torch.float16: _lib.JO_DTYPE_F16, torch.bfloat16: _lib.JO_DTYPE_BF16}
@@ -101,6 +102,32 @@ def fused_qk_norm_rope_3d_paired(q, k, seq_len, num_heads, eps, q_weight, k_weig
         _check(_L.jo_fused_qk_norm_rope_3d_paired(
             q.data_ptr(), k.data_ptr(), B, int(seq_len), int(num_heads), D, float(eps),
             q_weight.data_ptr(), k_weight.data_ptr(), cos.data_ptr(), sin.data_ptr(), st))
+
+
+def qk_norm_rope_strided(q, k, eps, q_weight, k_weight, cos=None, sin=None):
+    """In place on strided views q, k: [B, L, H, D] bf16 (last two dims dense,
+    tokens uniformly strided), e.g. ``qkv.view(B, L, 3, H, D)[:, :, 0]``.
+    Per-head RMSNorm with q/k weights, then interleaved-pair RoPE with
+    cos/sin [L, D/2] when given (norm only when cos is None).  Same arithmetic
+    as fused_qk_norm_rope_3d_paired, without copying q/k out of the QKV buffer."""
+    _chk(q.dim() == 4 and k.shape == q.shape, "q/k must be [B, L, H, D] views of the same shape")
+    B, L, H, D = q.shape
+    for t, n in ((q, "q"), (k, "k")):
+        _check_cuda(t, n)
+        _chk(t.dtype == torch.bfloat16, f"{n} dtype is {t.dtype}, expected torch.bfloat16")
+        _chk(t.stride(3) == 1 and t.stride(2) == D, f"{n}: heads must be dense [H, D]")
+        _chk(B == 1 or t.stride(0) == L * t.stride(1), f"{n}: tokens must be uniformly strided")
+    for t, n in ((q_weight, "q_weight"), (k_weight, "k_weight")):
+        _check_input(t, n, torch.bfloat16)
+    if cos is not None:
+        _check_input(cos, "cos", torch.bfloat16)
+        _check_input(sin, "sin", torch.bfloat16)
+        _chk(cos.shape == (L, D // 2) and sin.shape == (L, D // 2), "cos shape must be [seq_len, head_dim/2]")
+    with _Device(q) as st:
+        _check(_L.jo_qk_norm_rope_strided(
+            q.data_ptr(), k.data_ptr(), B, L, H, D, q.stride(1), k.stride(1), float(eps), q_weight.data_ptr(),
+            k_weight.data_ptr(), cos.data_ptr() if cos is not None else None,
+            sin.data_ptr() if sin is not None else None, st))
 
 
 # --------------------------------------------------------------------------

@@ -47,6 +47,7 @@ SIGNATURES = {
     "jo_last_error": [],
     "jo_device_arch": [_i32],
     "jo_fused_qk_norm_rope_3d_paired": [_p, _p, _i64, _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p],
+    "jo_qk_norm_rope_strided": [_p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p],
     "jo_fused_norm_scale_shift": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _p],
     "jo_rmsnorm": [_p, _p, _p, _i64, _i64, _i64, _f32, _i32, _p],
     "jo_per_token_quant_fp8": [_p, _i32, _p, _p, _i64, _i64, _p],

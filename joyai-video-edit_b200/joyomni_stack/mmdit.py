@@ -1,0 +1,265 @@
+"""Synthetic MMDiT double-stream block stack routed through joyomni_ops.
+
+This is the caller harness of BASELINE configs 4 and 5: the block arithmetic of
+the reference's ``MMDoubleStreamBlock.forward`` (deploy/xvideo/models/dit/dit.py:314-481)
+with every joyomni_ops call served by the sm_100a kernels of this repository,
+random-initialised weights and synthetic inputs.  Per block and stream:
+
+  mod  = modulate_table + vec -> shift1, scale1, gate1, shift2, scale2, gate2   (dit.py:112-125)
+  x_q  = per_token_fp8(LayerNorm(x) * (1 + scale1) + shift1)      fused entry  (dit.py:351-357 + fp8_linear.py:143-166)
+  qkv  = fp8_scaled_mm(x_q, W_qkv) + b                                          (fp8_linear.py:167)
+  q, k = RMSNorm_head + 3D RoPE, in place in the qkv buffer (image stream);     (dit.py:364-370)
+         RMSNorm_head only (text stream)                                        (dit.py:384-385)
+  attn = SDPA(q_img|q_txt, [k_cache | k_img | k_txt], [v ...])                   (dit.py:387-420)
+  x    = x + gate1 * fp8_linear(attn, W_proj)                                   (dit.py:463-466)
+  x    = x + gate2 * fp8_linear(gelu_tanh(fp8_linear(mod2(LN(x)), W_up)), W_down)  (dit.py:467-476)
+
+Differences from the reference model that the synthetic configuration asks
+for or that are harness simplifications: BASELINE's dims (hidden 5120, 40
+heads, FFN 13824, RoPE split 44/42/42); the KV cache stores post-RoPE keys of
+the image tokens of the last 2 chunks, written from the last denoising step
+(no separate clean-latent store forward); the latent <-> token projections and
+the Euler update act directly in token space.  Sequence parallelism (Ulysses,
+ulysses.py) is new; with P = 1 it degenerates to plain single-GPU execution.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+import torch.nn.functional as F
+
+import joyomni_ops as jo
+
+from .ulysses import SeqParallel
+
+NORM_EPS = 1e-6
+FP8 = torch.float8_e4m3fn
+
+
+@dataclass
+class StackConfig:
+    hidden: int = 5120
+    heads: int = 40
+    ffn: int = 13824
+    layers: int = 40
+    img_tokens: int = 10530          # 3 latent frames x 45 x 78 patches
+    txt_tokens: int = 512
+    grid: tuple = (3, 45, 78)        # (t, h, w) of the image tokens, row-major
+    rope_axes: tuple = (44, 42, 42)
+    rope_theta: float = 10000.0
+    cache_chunks: int = 2
+    seed: int = 5
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+
+def rope_tables(cfg: StackConfig, device) -> tuple:
+    """cos/sin [T*H*W, head_dim/2] bf16 for the row-major (t, h, w) grid:
+    per axis f_j = 1/theta^(2j/d), angle = pos * f_j (fp32); the de-duplicated
+    half of the repeat_interleaved tables (rope.py:31-52, sgl_fused_ops.py:87-94)."""
+    T, H, W = cfg.grid
+    tt, hh, ww = torch.meshgrid(torch.arange(T), torch.arange(H), torch.arange(W), indexing="ij")
+    cs, sn = [], []
+    for pos, d in zip((tt, hh, ww), cfg.rope_axes):
+        f = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2)[: d // 2].float() / d))
+        ang = torch.outer(pos.reshape(-1).float(), f)
+        cs.append(ang.cos())
+        sn.append(ang.sin())
+    return (torch.cat(cs, 1).to(torch.bfloat16).to(device).contiguous(),
+            torch.cat(sn, 1).to(torch.bfloat16).to(device).contiguous())
+
+
+class Fp8Weight:
+    """Per-output-channel FP8 weight in the reference's layout
+    (deploy/xvideo/models/dit/fp8_linear.py:100-110): column-major [K, N] e4m3
+    codes with scale = max(absmax_k |W[n, :]|, 1e-8) / 448, bias in bf16."""
+
+    def __init__(self, n: int, k: int, gen: torch.Generator, device, std: float = 0.02):
+        w = torch.randn((n, k), generator=gen, device=device, dtype=torch.bfloat16) * std
+        amax = w.abs().amax(dim=1).float().clamp_min(1e-8)
+        self.scale = (amax / 448.0).contiguous()
+        self.codes = (w.float() / self.scale[:, None]).clamp(-448, 448).to(FP8)   # [N, K] row-major
+        self.b = (torch.randn(n, generator=gen, device=device, dtype=torch.bfloat16) * 0.01).contiguous()
+        del w
+
+    @property
+    def t(self):  # column-major [K, N] view, as fp8_scaled_mm wants
+        return self.codes.t()
+
+    def __call__(self, xq, xs, gelu=False):
+        f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
+        return f(xq, self.t, xs, self.scale, torch.bfloat16, self.b)
+
+
+def quant(x):
+    q = torch.empty(x.shape, dtype=FP8, device=x.device)
+    s = torch.empty((x.shape[0], 1), dtype=torch.float32, device=x.device)
+    jo.sgl_per_token_quant_fp8(x, q, s)
+    return q, s
+
+
+def norm_mod_quant(x, shift, scale):
+    q = torch.empty(x.shape, dtype=FP8, device=x.device)
+    s = torch.empty((x.shape[0], 1), dtype=torch.float32, device=x.device)
+    jo.norm_modulate_quant_fp8(x, None, None, scale, shift, "layer", NORM_EPS, q, s)
+    return q, s
+
+
+class Stream:
+    """Weights of one stream (image or text) of one block."""
+
+    def __init__(self, cfg: StackConfig, gen, device):
+        D, Fh, Dh = cfg.hidden, cfg.ffn, cfg.head_dim
+        self.mod = (torch.randn((6, D), generator=gen, device=device) / math.sqrt(D)).to(torch.bfloat16)
+        self.qkv = Fp8Weight(3 * D, D, gen, device)
+        self.proj = Fp8Weight(D, D, gen, device)
+        self.up = Fp8Weight(Fh, D, gen, device)
+        self.down = Fp8Weight(D, Fh, gen, device)
+        self.q_norm = (1 + 0.1 * torch.randn(Dh, generator=gen, device=device)).to(torch.bfloat16)
+        self.k_norm = (1 + 0.1 * torch.randn(Dh, generator=gen, device=device)).to(torch.bfloat16)
+
+
+class LayerKV:
+    """Head-sharded K/V of one layer: [current | cache slot 0 | cache slot 1] along
+    tokens, so the all-to-all writes the current chunk's keys straight into the
+    buffer and the attention keys are one contiguous prefix."""
+
+    def __init__(self, cfg: StackConfig, sp: SeqParallel, device):
+        self.cap = cfg.cache_chunks * cfg.img_tokens
+        n = sp.total_len + self.cap
+        self.k = torch.empty((n, sp.local_heads, cfg.head_dim), dtype=torch.bfloat16, device=device)
+        self.v = torch.empty_like(self.k)
+        self.valid = 0          # cached image tokens
+        self.next_slot = 0
+        self.cur = sp.total_len
+        self.img_len = cfg.img_tokens
+
+    def keys(self):
+        n = self.cur + self.valid
+        return self.k[:n], self.v[:n]
+
+    def commit(self, sp: SeqParallel):
+        """Store the current chunk's image-token K/V into the ring (oldest slot)."""
+        base = self.cur + self.next_slot * self.img_len
+        off = 0
+        for start, length in sp.gathered_img_segments():
+            self.k[base + off: base + off + length].copy_(self.k[start:start + length])
+            self.v[base + off: base + off + length].copy_(self.v[start:start + length])
+            off += length
+        self.next_slot = (self.next_slot + 1) % (self.cap // self.img_len)
+        self.valid = min(self.cap, self.valid + self.img_len)
+
+    def fill_random(self, gen, chunks: int):
+        """Pre-fill `chunks` cache slots with N(0,1) K/V."""
+        n = chunks * self.img_len
+        self.k[self.cur:self.cur + n].normal_(generator=gen)
+        self.v[self.cur:self.cur + n].normal_(generator=gen)
+        self.valid = n
+        self.next_slot = chunks % (self.cap // self.img_len)
+
+
+class Block:
+    def __init__(self, cfg: StackConfig, gen, device):
+        self.cfg = cfg
+        self.img = Stream(cfg, gen, device)
+        self.txt = Stream(cfg, gen, device)
+
+    def forward(self, img, txt, vec, cos, sin, kv: LayerKV, sp: SeqParallel):
+        cfg = self.cfg
+        H, Dh, D = cfg.heads, cfg.head_dim, cfg.hidden
+        Li, Lt = img.shape[0], txt.shape[0]
+        im = (self.img.mod + vec).unbind(0)
+        tm = (self.txt.mod + vec).unbind(0)
+
+        # ---- QKV, per stream, on this rank's tokens -----------------------
+        xq, xs = norm_mod_quant(img, im[0], im[1])
+        iqkv = self.img.qkv(xq, xs).view(1, Li, 3, H, Dh)
+        jo.qk_norm_rope_strided(iqkv[:, :, 0], iqkv[:, :, 1], NORM_EPS, self.img.q_norm, self.img.k_norm, cos, sin)
+        tq, ts = norm_mod_quant(txt, tm[0], tm[1])
+        tqkv = self.txt.qkv(tq, ts).view(1, Lt, 3, H, Dh)
+        jo.qk_norm_rope_strided(tqkv[:, :, 0], tqkv[:, :, 1], NORM_EPS, self.txt.q_norm, self.txt.k_norm)
+
+        # ---- attention over [current | cached] keys, head-sharded ------------
+        def cat_seq(i):
+            return torch.cat((iqkv[0, :, i], tqkv[0, :, i]), 0)             # [L_local, H, Dh]
+
+        q = sp.seq_to_heads(cat_seq(0))
+        sp.seq_to_heads(cat_seq(1), out=kv.k[:kv.cur])
+        sp.seq_to_heads(cat_seq(2), out=kv.v[:kv.cur])
+        k_all, v_all = kv.keys()
+        with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
+                                             torch.nn.attention.SDPBackend.FLASH_ATTENTION,
+                                             torch.nn.attention.SDPBackend.EFFICIENT_ATTENTION]):
+            o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k_all.permute(1, 0, 2)[None],
+                                               v_all.permute(1, 0, 2)[None])
+        o = sp.heads_to_seq(o[0].permute(1, 0, 2)).reshape(Li + Lt, D)
+
+        # ---- projections + FFN with gated residuals ------------------------
+        img = self._tail(self.img, im, img, o[:Li])
+        txt = self._tail(self.txt, tm, txt, o[Li:])
+        return img, txt
+
+    @staticmethod
+    def _tail(st: Stream, m, x, attn):
+        aq, as_ = quant(attn)
+        x = torch.addcmul(x, st.proj(aq, as_), m[2])
+        hq, hs = norm_mod_quant(x, m[3], m[4])
+        h = st.up(hq, hs, gelu=True)
+        h2q, h2s = quant(h)
+        return torch.addcmul(x, st.down(h2q, h2s), m[5])
+
+
+class Stack:
+    """cfg.layers blocks, per-layer head-sharded KV cache, chunk-causal loop."""
+
+    def __init__(self, cfg: StackConfig, device, sp: Optional[SeqParallel] = None, layers: Optional[int] = None):
+        self.cfg = cfg
+        self.device = device
+        self.sp = sp or SeqParallel.create(cfg.img_tokens, cfg.txt_tokens, cfg.heads)
+        gen = torch.Generator(device=device).manual_seed(cfg.seed)
+        n = cfg.layers if layers is None else layers
+        self.blocks: List[Block] = [Block(cfg, gen, device) for _ in range(n)]
+        self.kv = [LayerKV(cfg, self.sp, device) for _ in range(n)]
+        cos, sin = rope_tables(cfg, device)
+        a, b = self.sp.img_range
+        self.cos, self.sin = cos[a:b].contiguous(), sin[a:b].contiguous()
+
+    def forward(self, img, txt, vec):
+        for blk, kv in zip(self.blocks, self.kv):
+            img, txt = blk.forward(img, txt, vec, self.cos, self.sin, kv, self.sp)
+        return img, txt
+
+    def commit_kv(self):
+        for kv in self.kv:
+            kv.commit(self.sp)
+
+    def inputs(self, seed: int):
+        """This rank's shard of a chunk's synthetic inputs (identical global
+        tensors on every rank): image latents in token space (fp32), text tokens
+        and the timestep embedding, all N(0, 1)."""
+        cfg = self.cfg
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        img = torch.randn((cfg.img_tokens, cfg.hidden), generator=g)
+        txt = torch.randn((cfg.txt_tokens, cfg.hidden), generator=g)
+        a, b = self.sp.img_range
+        c, d = self.sp.txt_range
+        return (img[a:b].to(self.device), txt[c:d].to(torch.bfloat16).to(self.device))
+
+    def timestep_vec(self, t: float):
+        g = torch.Generator(device="cpu").manual_seed(int(t) * 7919 + 1)
+        return torch.randn(self.cfg.hidden, generator=g).to(torch.bfloat16).to(self.device)
+
+    def denoise_chunk(self, x: torch.Tensor, txt: torch.Tensor, timesteps=(1000, 750, 500)):
+        """3 denoising steps (Euler in fp32 over sigmas t/1000 -> next, last -> 0);
+        the chunk's image K/V from the last step enter the cache afterwards."""
+        sig = [t / 1000.0 for t in timesteps] + [0.0]
+        for i, t in enumerate(timesteps):
+            v, _ = self.forward(x.to(torch.bfloat16), txt, self.timestep_vec(t))
+            x = x + (sig[i + 1] - sig[i]) * v.float()
+        self.commit_kv()
+        return x

@@ -5,7 +5,7 @@ import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(REPO, "joyai-video-edit_b200")
-for p in (PKG, os.path.join(REPO, "oracle"), REPO):
+for p in (PKG, os.path.join(REPO, "oracle"), REPO, os.path.dirname(os.path.abspath(__file__))):
     if p not in sys.path:
         sys.path.insert(0, p)
 

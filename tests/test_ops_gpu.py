@@ -247,3 +247,31 @@ def test_kernels_against_reference_golden(jo, cuda, path):
         # same reduction tree and expression forms as the reference kernel
         fr = golden_cases.exact_fraction(got, ref)
         assert min(fr.values()) == 1.0, fr
+
+
+# ------------------------------------------------ strided qk norm (+rope) --
+@pytest.mark.parametrize("rope", [True, False])
+def test_qk_norm_rope_strided_matches_dense(jo, cuda, rope):
+    """In place on the q/k thirds of a [L, 3, H, D] QKV buffer; identical bits to
+    the dense entry on copies, v untouched."""
+    rng = np.random.default_rng(91)
+    L, H, D = 64, 5, 128
+    qkv = to_torch(randn(rng, (L, 3, H, D)), "bf16", cuda)
+    qw = to_torch(O.round_bf16(1 + 0.1 * rng.standard_normal(D).astype(np.float32)), "bf16", cuda)
+    kw = to_torch(O.round_bf16(1 + 0.1 * rng.standard_normal(D).astype(np.float32)), "bf16", cuda)
+    c, s = O.rope_tables_3d((1, 8, 8))
+    ct, st_ = to_torch(c, "bf16", cuda), to_torch(s, "bf16", cuda)
+    v0 = qkv[:, 2].clone()
+    q_ref = qkv[:, 0].contiguous().view(1, L * H, D)
+    k_ref = qkv[:, 1].contiguous().view(1, L * H, D)
+    view = qkv.view(1, L, 3, H, D)
+    if rope:
+        jo.fused_qk_norm_rope_3d_paired(q_ref, k_ref, L, H, 1e-6, qw, kw, ct, st_)
+        jo.qk_norm_rope_strided(view[:, :, 0], view[:, :, 1], 1e-6, qw, kw, ct, st_)
+        assert torch.equal(qkv[:, 0].reshape(1, L * H, D), q_ref)
+        assert torch.equal(qkv[:, 1].reshape(1, L * H, D), k_ref)
+    else:
+        jo.qk_norm_rope_strided(view[:, :, 0], view[:, :, 1], 1e-6, qw, kw)
+        ref = O.rmsnorm(to_np(q_ref).reshape(L * H, D), to_np(qw), 1e-6)
+        assert_close_ulp(to_np(qkv[:, 0]).reshape(L * H, D), ref)
+    assert torch.equal(qkv[:, 2], v0)

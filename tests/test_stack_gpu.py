@@ -1,0 +1,71 @@
+"""GPU checks of the MMDiT block-stack harness (BASELINE configs 4/5) built on
+joyomni_ops: one block against an eager-torch restatement of the reference
+block (relative RMS <= 1e-2, the stated block tolerance), the KV-cache ring,
+and (with >= 2 GPUs) Ulysses P = 2 against P = 1 (relative RMS <= 1e-3)."""
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+import stack_reference as R
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _small_cfg(**kw):
+    from joyomni_stack import StackConfig
+    base = dict(hidden=512, heads=4, ffn=1376, layers=2, img_tokens=130, txt_tokens=24, grid=(1, 10, 13),
+                cache_chunks=2, seed=11)
+    base.update(kw)
+    return StackConfig(**base)
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).pow(2).mean().sqrt() / b.pow(2).mean().sqrt()).item()
+
+
+@pytest.mark.parametrize("hidden,heads,ffn", [(512, 4, 1376), (1024, 8, 2752)])
+def test_block_matches_eager_reference(cuda, hidden, heads, ffn):
+    from joyomni_stack import Stack
+    cfg = _small_cfg(hidden=hidden, heads=heads, ffn=ffn, layers=1)
+    st = Stack(cfg, cuda)
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    st.kv[0].fill_random(gen, 2)
+    img, txt = st.inputs(7)
+    img = img.to(torch.bfloat16)
+    vec = st.timestep_vec(1000)
+    ck = st.kv[0].k[st.kv[0].cur: st.kv[0].cur + st.kv[0].valid].clone()
+    cv = st.kv[0].v[st.kv[0].cur: st.kv[0].cur + st.kv[0].valid].clone()
+    ref_img, ref_txt, _, _ = R.block_forward(st.blocks[0], img, txt, vec, st.cos, st.sin, ck, cv)
+    out_img, out_txt = st.blocks[0].forward(img, txt, vec, st.cos, st.sin, st.kv[0], st.sp)
+    assert torch.isfinite(out_img).all() and torch.isfinite(out_txt).all()
+    assert _rel(out_img, ref_img) <= 1e-2
+    assert _rel(out_txt, ref_txt) <= 1e-2
+
+
+def test_kv_cache_ring(cuda):
+    from joyomni_stack import Stack
+    cfg = _small_cfg(layers=1)
+    st = Stack(cfg, cuda)
+    x, txt = st.inputs(1)
+    for chunk in range(3):
+        x = st.denoise_chunk(x, txt)
+        kv = st.kv[0]
+        assert kv.valid == min(chunk + 1, 2) * cfg.img_tokens
+    assert torch.isfinite(x).all()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ulysses_two_gpus_matches_one(cuda):
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([os.path.join(REPO, "joyai-video-edit_b200"),
+                                                        os.path.join(REPO, "tests")]))
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr=127.0.0.1", "--master-port=29517", os.path.join(REPO, "tests", "_stack_mp.py")],
+                       capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "ULYSSES_OK" in r.stdout, r.stdout[-2000:]

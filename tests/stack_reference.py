@@ -12,8 +12,9 @@ def quant(y):
     """per_token_quant_fp8.cu:55-78 in torch: y bf16 [M, K] -> (codes as float, scale [M, 1])."""
     yf = y.float()
     amax = yf.abs().amax(-1, keepdim=True)
-    s = amax / 448.0
-    inv = torch.where(s == 0, torch.zeros_like(s), 1.0 / s)
+    s = (amax.double() / 448.0).float()   # IEEE amax/448 (torch's GPU scalar division multiplies by 1/448)
+    # correctly rounded 1/s (the kernel's IEEE reciprocal); float64 then round
+    inv = torch.where(s == 0, torch.zeros_like(s), (1.0 / s.double()).float())
     q = (yf * inv).clamp(-448, 448).to(torch.float8_e4m3fn).float()
     return q, s
 
@@ -59,8 +60,9 @@ def block_forward(blk, img, txt, vec, cos, sin, cache_k=None, cache_v=None):
     if cache_k is not None:
         k = torch.cat((k, cache_k), 0)
         v = torch.cat((v, cache_v), 0)
-    o = F.scaled_dot_product_attention(q.float().permute(1, 0, 2)[None], k.float().permute(1, 0, 2)[None],
-                                       v.float().permute(1, 0, 2)[None])[0].permute(1, 0, 2)
+    # bf16 attention, as the reference model runs it (FA4 / SDPA in bf16, dit.py:162-178)
+    o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None],
+                                       v.permute(1, 0, 2)[None])[0].permute(1, 0, 2)
     o = o.reshape(-1, D).to(torch.bfloat16)
 
     def tail(st, m, x, attn):

@@ -275,3 +275,26 @@ def test_qk_norm_rope_strided_matches_dense(jo, cuda, rope):
         ref = O.rmsnorm(to_np(q_ref).reshape(L * H, D), to_np(qw), 1e-6)
         assert_close_ulp(to_np(qkv[:, 0]).reshape(L * H, D), ref)
     assert torch.equal(qkv[:, 2], v0)
+
+
+@pytest.mark.parametrize("M,N", [(37, 1024), (130, 5120), (9, 2048), (3, 13824)])
+@pytest.mark.parametrize("nt", [0, 1])
+@pytest.mark.parametrize("affine", [False, True])
+def test_broadcast_modulation_paths(jo, cuda, M, N, nt, affine):
+    """[N] shift/scale (the model's adaLN layout): fused norm->quant and
+    norm->modulate through the staged kernel, against the oracle."""
+    rng = np.random.default_rng(M + N + nt * 3 + affine)
+    x = outlier_activations(rng, M, N)
+    sc, sh = randn(rng, (N,), 0.1), randn(rng, (N,), 0.1)
+    g = O.round_bf16(1 + 0.1 * rng.standard_normal(N).astype(np.float32)) if affine else None
+    b = randn(rng, (N,), 0.1) if affine else None
+    T = lambda a: None if a is None else to_torch(a, "bf16", cuda)  # noqa: E731
+    yo = O.fused_norm_scale_shift(x, g, b, sc, sh, nt, 1e-6)
+    y = jo.fused_norm_scale_shift(T(x), T(g), T(b), T(sc).expand(M, N), T(sh).expand(M, N), nt, 1e-6)
+    assert_close_ulp(to_np(y), yo)
+    q = torch.empty((M, N), dtype=torch.float8_e4m3fn, device=cuda)
+    s = torch.empty(M, dtype=torch.float32, device=cuda)
+    jo.norm_modulate_quant_fp8(T(x), T(g), T(b), T(sc), T(sh), nt, 1e-6, q, s)
+    rq, rs = O.per_token_quant_fp8(to_np(y))
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(codes_np(q), rq)

@@ -255,6 +255,11 @@ def run_ours(args):
         e2e_ms = float(t.item())
     e2e_val = bytes_step * K * world / (e2e_ms * 1e-3) / 1e9
 
+    stack = None
+    if not args.no_stack:
+        del xs, qs, ss, xd
+        torch.cuda.empty_cache()
+        stack = stack_bench(torch, dev, world)
     kernels = {}
     ref_gpu = None
     cpu = None
@@ -285,6 +290,8 @@ def run_ours(args):
                          "avg_launch_us": round(avg_launch_us, 3)},
             "clocks": clocks,
         }
+        if stack is not None:
+            line["stack"] = stack
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if kernels:
@@ -295,6 +302,62 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def stack_bench(torch, dev, world):
+    """BASELINE configs 4 and 5 on this N: the 40-layer synthetic MMDiT stack
+    (hidden 5120, 40 heads, FFN 13824, 10530 image + 512 text tokens, KV cache of
+    2 previous chunks pre-filled with N(0,1)), Ulysses over all ranks.  Times one
+    block forward (config 4 at N = 1) and one chunk = 3 denoising steps x 40
+    layers + KV commit (config 5) after one warm chunk; max over ranks."""
+    import torch.distributed as dist
+    from joyomni_stack import Stack, StackConfig
+    cfg = StackConfig()
+    st = Stack(cfg, dev)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    for kv in st.kv:
+        kv.fill_random(gen, cfg.cache_chunks)
+    x, txt = st.inputs(1)
+    vec = st.timestep_vec(1000)
+    xb = x.to(torch.bfloat16)
+
+    def timed(fn, reps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    blk = lambda: st.blocks[0].forward(xb, txt, vec, st.cos, st.sin, st.kv[0], st.sp)  # noqa: E731
+    blk()
+    blk()
+    block_ms = timed(blk, 5)
+    state = {"x": st.denoise_chunk(x, txt)}          # warm chunk (cache stays full: commit rotates slots)
+
+    def chunk():
+        state["x"] = st.denoise_chunk(state["x"], txt)
+    chunk_ms = timed(chunk, 1)
+    finite = bool(torch.isfinite(state["x"]).all())
+    gflop_block = 2 * (cfg.img_tokens + cfg.txt_tokens) * cfg.hidden * (4 * cfg.hidden + 2 * cfg.ffn) / 1e9
+    attn_flop = 4 * (cfg.img_tokens + cfg.txt_tokens) * (cfg.img_tokens * 3 + cfg.txt_tokens) * cfg.hidden / 1e9
+    out = {"config": "cfg4 block / cfg5 40 layers x 3 steps, 10530 img + 512 txt tokens, KV 2 chunks (post-RoPE)",
+           "ulysses_degree": world, "block_ms": round(block_ms, 2), "chunk_ms": round(chunk_ms, 1),
+           "fps": round(24 / (chunk_ms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
+           "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
+           "attention": "torch SDPA (cuDNN/flash), bf16"}
+    del st
+    torch.cuda.empty_cache()
+    return out
 
 
 def kernel_table(torch, jo, dev):
@@ -495,6 +558,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip per-kernel table / CPU baseline")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 40-layer block-stack timing")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per launch, if measured")
     args = ap.parse_args()

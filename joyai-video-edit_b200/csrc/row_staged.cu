@@ -27,10 +27,13 @@
 // saturation of the e4m3 conversion.
 #include "jo_common.cuh"
 
+#include <stdlib.h>
+
 namespace jo {
 namespace staged {
 
 enum : int { OP_NORM_MOD = 0, OP_QUANT = 2, OP_NORM_MOD_QUANT = 3 };
+constexpr int kMaxTeams = 15;  // teams per CTA (named barriers 1..15)
 
 struct Args {
   const void* x;
@@ -72,6 +75,16 @@ __device__ __forceinline__ float4 lds16f(const float* p) {
                : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
                : "r"((unsigned)__cvta_generic_to_shared(p)));
   return r;
+}
+
+// Unpack two bf16/fp16 from a word.  The bf16 form is an opaque (volatile)
+// asm so each use recomputes it: keeping fp32 copies of a whole row alive
+// across the row reduction would cost 2 registers per element.
+template <typename T> __device__ __forceinline__ float2 unpack2_r(uint32_t w) { return unpack2<T>(w); }
+template <> __device__ __forceinline__ float2 unpack2_r<__nv_bfloat16>(uint32_t w) {
+  uint32_t lo, hi;
+  asm volatile("shl.b32 %0, %2, 16;\n\tand.b32 %1, %2, 0xffff0000;" : "=r"(lo), "=r"(hi) : "r"(w));
+  return make_float2(__uint_as_float(lo), __uint_as_float(hi));
 }
 
 // Team-wide reductions of R independent values (one per row).  Warp shuffles
@@ -225,11 +238,13 @@ __device__ __forceinline__ void quant_rows(const Vec16<T> (&X)[R][VPL], const ui
   }
 }
 
+constexpr int staged_max_threads(int vpl, int r) { return vpl * r >= 10 ? 256 : vpl * r == 8 ? 640 : 512; }
+
 template <typename T, int OP, int NORM, int VPL, int S, int R>
-__global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int team, const int teams) {
+__global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
+    staged_rows(const Args a, const int team, const int teams) {
   constexpr bool HAS_NORM = (OP != OP_QUANT);
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ float red[15][2][4][R * 16];
 
   const int N = a.N;
   const int nvec = N / 8;
@@ -246,6 +261,11 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
   float* tb = tsh + N;                                  // beta (layer norm only)
   uint4* ring = reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) +
                 (size_t)tm * S * R * nvec;
+  // per-team reduction scratch [2 parities][4 slots][R * 16] after all rings
+  typedef float RedT[4][R * 16];
+  RedT* red = reinterpret_cast<RedT*>(reinterpret_cast<float*>(
+                  reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) + (size_t)teams * S * R * nvec)) +
+              (size_t)tm * 2;
   if constexpr (HAS_NORM) {
     const bool has_g = a.gamma != nullptr;
     const bool has_b = NORM == JO_NORM_LAYER && has_g && a.beta != nullptr;
@@ -253,11 +273,16 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
     const T* b = static_cast<const T*>(a.beta);
     const T* sc = static_cast<const T*>(a.scale);
     const T* sh = static_cast<const T*>(a.shift);
+    // Bank-conflict-free layout: element c = 8*v + 4*h + e of a table is
+    // stored at h*(N/2) + 4*v + e, so the 16-byte reads of consecutive threads
+    // (consecutive v, same h) are contiguous.
     for (int i = tid; i < N; i += blockDim.x) {
-      tg[i] = has_g ? to_f32(g[i]) : 1.f;
-      if (NORM == JO_NORM_LAYER) tb[i] = has_b ? to_f32(b[i]) : 0.f;
-      tsc[i] = 1.f + to_f32(sc[i]);
-      tsh[i] = to_f32(sh[i]);
+      const int v = i >> 3, h = (i >> 2) & 1, e = i & 3;
+      const int d = h * (N >> 1) + 4 * v + e;
+      tg[d] = has_g ? to_f32(g[i]) : 1.f;
+      if (NORM == JO_NORM_LAYER) tb[d] = has_b ? to_f32(b[i]) : 0.f;
+      tsc[d] = 1.f + to_f32(sc[i]);
+      tsh[d] = to_f32(sh[i]);
     }
     __syncthreads();
   }
@@ -326,8 +351,8 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
         }
         bits[r] = absmax2_fold(acc);
       }
-      team_umax<R>(bits, team, bar_id, red[tm][parity][0]);
-      quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[tm][parity][1]);
+      team_umax<R>(bits, team, bar_id, red[parity][0]);
+      quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[parity][1]);
     } else {
       float mean[R], rr[R];
       if constexpr (NORM == JO_NORM_LAYER) {
@@ -340,13 +365,13 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
             const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack2<T>(w[k]);
+              const float2 f = unpack2_r<T>(w[k]);
               sum[r] += f.x;
               sum[r] += f.y;
             }
           }
         }
-        team_sum<R>(sum, team, bar_id, red[tm][parity][0]);
+        team_sum<R>(sum, team, bar_id, red[parity][0]);
         float ss[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -358,14 +383,14 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
               const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const float2 f = unpack2<T>(w[k]);
+                const float2 f = unpack2_r<T>(w[k]);
                 const float d0 = f.x - mean[r], d1 = f.y - mean[r];
                 ss[r] = fmaf(d0, d0, ss[r]);
                 ss[r] = fmaf(d1, d1, ss[r]);
               }
             }
         }
-        team_sum<R>(ss, team, bar_id, red[tm][parity][1]);
+        team_sum<R>(ss, team, bar_id, red[parity][1]);
 #pragma unroll
         for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
       } else {
@@ -379,13 +404,13 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
             const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack2<T>(w[k]);
+              const float2 f = unpack2_r<T>(w[k]);
               ss[r] = fmaf(f.x, f.x, ss[r]);
               ss[r] = fmaf(f.y, f.y, ss[r]);
             }
           }
         }
-        team_sum<R>(ss, team, bar_id, red[tm][parity][0]);
+        team_sum<R>(ss, team, bar_id, red[parity][0]);
 #pragma unroll
         for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
       }
@@ -398,7 +423,7 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
         if (idx >= nvec) continue;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int c = idx * 8 + 4 * h;
+          const int c = h * (N >> 1) + 4 * idx;
           const float4 g = lds16f(tg + c);
           const float4 sc = lds16f(tsc + c);
           const float4 sh = lds16f(tsh + c);
@@ -407,8 +432,8 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             uint32_t* wr = reinterpret_cast<uint32_t*>(&X[r][i].raw);
-            const float2 f0 = unpack2<T>(wr[2 * h]);
-            const float2 f1 = unpack2<T>(wr[2 * h + 1]);
+            const float2 f0 = unpack2_r<T>(wr[2 * h]);
+            const float2 f1 = unpack2_r<T>(wr[2 * h + 1]);
             const float m = mean[r], rv = rr[r];
             float y0, y1, y2, y3;
             if constexpr (NORM == JO_NORM_LAYER) {
@@ -446,8 +471,8 @@ __global__ void __launch_bounds__(512, 1) staged_rows(const Args a, const int te
         uint32_t bits[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) bits[r] = absmax2_fold(acc[r]);
-        team_umax<R>(bits, team, bar_id, red[tm][parity][2]);
-        quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[tm][parity][3]);
+        team_umax<R>(bits, team, bar_id, red[parity][2]);
+        quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[parity][3]);
       }
     }
   }
@@ -458,13 +483,13 @@ template <typename T, int OP, int NORM, int VPL, int S, int R>
 int launch(const Args& a, int team, cudaStream_t st) {
   const int nvec = a.N / 8;
   const size_t tab = (OP != OP_QUANT) ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
-  const size_t per_team = (size_t)S * R * nvec * 16;
+  const size_t per_team = (size_t)S * R * nvec * 16 + (size_t)2 * 4 * R * 16 * sizeof(float);
   // Up to 512 threads and ~200 KB of shared memory per CTA, one CTA per SM.
-  int teams = 512 / team;
-  if (teams > 15) teams = 15;   // named barriers 1..15
-  while (teams > 1 && tab + teams * per_team > 200 * 1024) --teams;
+  int teams = staged_max_threads(VPL, R) / team;
+  if (teams > kMaxTeams) teams = kMaxTeams;
+  while (teams > 1 && tab + teams * per_team > 224 * 1024) --teams;
   const size_t smem = tab + teams * per_team;
-  if (smem > 200 * 1024) return JO_ERR_INVALID;
+  if (smem > 224 * 1024) return JO_ERR_INVALID;
   static size_t attr = 0;
   if (attr < smem) {
     cudaFuncSetAttribute(staged_rows<T, OP, NORM, VPL, S, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -479,6 +504,49 @@ int launch(const Args& a, int team, cudaStream_t st) {
 
 }  // namespace staged
 
+// Geometry of the staged kernel: vectors per thread, rows per team
+// iteration, ring stages.  The team spans the row (ceil32(nvec / vpl) threads).
+struct StagedGeom {
+  int vpl, r, s;
+};
+
+static StagedGeom pick_geom(int nvec) {
+  // JO_STAGED_GEOM="vpl,r,s" overrides the choice (used to compare geometries).
+  static int ov = -1;
+  static StagedGeom g_ov{4, 2, 2};
+  if (ov < 0) {
+    ov = 0;
+    if (const char* e = getenv("JO_STAGED_GEOM")) {
+      int v, r, st;
+      if (sscanf(e, "%d,%d,%d", &v, &r, &st) == 3) {
+        g_ov = StagedGeom{v, r, st};
+        ov = 1;
+      }
+    }
+  }
+  if (ov == 1) return g_ov;
+  (void)nvec;
+  return StagedGeom{4, 2, 2};
+}
+
+template <typename T, int OP, int NORM>
+static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream_t st) {
+  using namespace staged;
+  const int team = ((nvec + g.vpl - 1) / g.vpl + 31) / 32 * 32;
+  if (team > 512) return JO_ERR_INVALID;
+#define JO_G(V, R, S) \
+  if (g.vpl == V && g.r == R && g.s == S) return launch<T, OP, NORM, V, S, R>(a, team, st);
+  JO_G(4, 2, 2)
+  JO_G(4, 1, 3)
+  JO_G(10, 1, 2)
+  JO_G(10, 1, 3)
+  JO_G(20, 1, 2)
+  JO_G(20, 1, 3)
+  JO_G(8, 2, 2)
+#undef JO_G
+  return launch<T, OP, NORM, 4, 2, 2>(a, ((nvec + 3) / 4 + 31) / 32 * 32, st);
+}
+
 // Entry used by row_ops.cu.  Returns JO_ERR_INVALID (no launch) when the shape
 // is not covered, so the caller falls back to the register kernel.
 int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, const void* gamma, const void* beta,
@@ -488,19 +556,17 @@ int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, cons
   if (dtype != JO_DTYPE_BF16 && dtype != JO_DTYPE_F16) return JO_ERR_INVALID;
   const int nvec = N / 8;
   if (N % 8 != 0 || nvec < 128) return JO_ERR_INVALID;
-  const int team = ((nvec + 3) / 4 + 31) / 32 * 32;   // 4 vectors per thread
-  if (team > 512) return JO_ERR_INVALID;
   Args a{x, y, gamma, beta, scale, shift, q, s, M, N, eps};
-  constexpr int S = 2, R = 2;
+  const StagedGeom g = pick_geom(nvec);
 #define JO_ST(T)                                                                                          \
   do {                                                                                                    \
-    if (op == OP_QUANT) return launch<T, OP_QUANT, JO_NORM_RMS, 4, S, R>(a, team, st);                   \
+    if (op == OP_QUANT) return launch_geom<T, OP_QUANT, JO_NORM_RMS>(a, nvec, g, st);                    \
     if (op == OP_NORM_MOD_QUANT)                                                                          \
-      return norm == JO_NORM_RMS ? launch<T, OP_NORM_MOD_QUANT, JO_NORM_RMS, 4, S, R>(a, team, st)       \
-                                 : launch<T, OP_NORM_MOD_QUANT, JO_NORM_LAYER, 4, S, R>(a, team, st);    \
+      return norm == JO_NORM_RMS ? launch_geom<T, OP_NORM_MOD_QUANT, JO_NORM_RMS>(a, nvec, g, st)        \
+                                 : launch_geom<T, OP_NORM_MOD_QUANT, JO_NORM_LAYER>(a, nvec, g, st);     \
     if (op == OP_NORM_MOD)                                                                                \
-      return norm == JO_NORM_RMS ? launch<T, OP_NORM_MOD, JO_NORM_RMS, 4, S, R>(a, team, st)             \
-                                 : launch<T, OP_NORM_MOD, JO_NORM_LAYER, 4, S, R>(a, team, st);          \
+      return norm == JO_NORM_RMS ? launch_geom<T, OP_NORM_MOD, JO_NORM_RMS>(a, nvec, g, st)              \
+                                 : launch_geom<T, OP_NORM_MOD, JO_NORM_LAYER>(a, nvec, g, st);           \
   } while (0)
   if (dtype == JO_DTYPE_BF16) JO_ST(__nv_bfloat16);
   else JO_ST(__half);

@@ -219,34 +219,40 @@ __global__ void __launch_bounds__(256, 2) row_kernel(const RowArgs a, const int 
     } else {
       // ---- statistics -----------------------------------------------------
       float mean = 0.f, r;
+      // Two fp32 chains per thread (even / odd element of each pair), added
+      // before the team reduction -- the same order as the staged kernel.
       if constexpr (NORM == JO_NORM_LAYER) {
-        float sum = 0.f;
+        float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < VPL; ++i)
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) sum += X[i].get(j);
-        sum = team_reduce<false>(sum, team, rs);
+          for (int j = 0; j < VEC; j += 2) s2 = add2(s2, make_float2(X[i].get(j), X[i].get(j + 1)));
+        float sum = team_reduce<false>(s2.x + s2.y, team, rs);
         mean = sum / (float)N;
-        float ss = 0.f;
+        float2 q2 = make_float2(0.f, 0.f);
+        const float2 nm = make_float2(-mean, -mean);
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
           if (i * team + tl < nvec) {
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-              const float d = X[i].get(j) - mean;
-              ss = fmaf(d, d, ss);
+            for (int j = 0; j < VEC; j += 2) {
+              const float2 d = add2(make_float2(X[i].get(j), X[i].get(j + 1)), nm);
+              q2 = fma2(d, d, q2);
             }
           }
         }
-        ss = team_reduce<false>(ss, team, red[parity][1]);
+        const float ss = team_reduce<false>(q2.x + q2.y, team, red[parity][1]);
         r = rsqrtf(ss / (float)N + a.eps);
       } else {
-        float ss = 0.f;
+        float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < VPL; ++i)
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) ss = fmaf(X[i].get(j), X[i].get(j), ss);
-        ss = team_reduce<false>(ss, team, rs);
+          for (int j = 0; j < VEC; j += 2) {
+            const float2 f = make_float2(X[i].get(j), X[i].get(j + 1));
+            q2 = fma2(f, f, q2);
+          }
+        const float ss = team_reduce<false>(q2.x + q2.y, team, rs);
         r = rsqrtf(ss / (float)N + a.eps);
       }
       // ---- elementwise (in place in X, rounded to T) ----------------------

@@ -171,7 +171,10 @@ __device__ __forceinline__ uint2 codes8(const uint4& v, float inv) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const float2 f = unpack2<T>(w[k]);
-    if (FAST) c[k] = pack_e4m3x2(__fmul_rn(f.x, inv), __fmul_rn(f.y, inv));
+    if (FAST) {
+      const float2 v = mul2(f, make_float2(inv, inv));
+      c[k] = pack_e4m3x2(v.x, v.y);
+    }
     else c[k] = pack_e4m3x2(qval(f.x, inv), qval(f.y, inv));
   }
   return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
@@ -354,41 +357,41 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
       team_umax<R>(bits, team, bar_id, red[parity][0]);
       quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[parity][1]);
     } else {
+      // Row statistics: each thread accumulates its elements in two fp32
+      // chains (even / odd element of every pair, one paired instruction per
+      // pair), the chains are added, then the team reduces.
       float mean[R], rr[R];
       if constexpr (NORM == JO_NORM_LAYER) {
         float sum[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          sum[r] = 0.f;
+          float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < VPL; ++i) {
             const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack2_r<T>(w[k]);
-              sum[r] += f.x;
-              sum[r] += f.y;
-            }
+            for (int k = 0; k < 4; ++k) s2 = add2(s2, unpack2_r<T>(w[k]));
           }
+          sum[r] = s2.x + s2.y;
         }
         team_sum<R>(sum, team, bar_id, red[parity][0]);
         float ss[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           mean[r] = sum[r] / (float)N;
-          ss[r] = 0.f;
+          const float2 nm = make_float2(-mean[r], -mean[r]);
+          float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < VPL; ++i)
             if (i * team + tl < nvec) {
               const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const float2 f = unpack2_r<T>(w[k]);
-                const float d0 = f.x - mean[r], d1 = f.y - mean[r];
-                ss[r] = fmaf(d0, d0, ss[r]);
-                ss[r] = fmaf(d1, d1, ss[r]);
+                const float2 d = add2(unpack2_r<T>(w[k]), nm);
+                q2 = fma2(d, d, q2);
               }
             }
+          ss[r] = q2.x + q2.y;
         }
         team_sum<R>(ss, team, bar_id, red[parity][1]);
 #pragma unroll
@@ -398,22 +401,25 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           mean[r] = 0.f;
-          ss[r] = 0.f;
+          float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < VPL; ++i) {
             const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const float2 f = unpack2_r<T>(w[k]);
-              ss[r] = fmaf(f.x, f.x, ss[r]);
-              ss[r] = fmaf(f.y, f.y, ss[r]);
+              q2 = fma2(f, f, q2);
             }
           }
+          ss[r] = q2.x + q2.y;
         }
         team_sum<R>(ss, team, bar_id, red[parity][0]);
 #pragma unroll
         for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
       }
+      // y = ((x - mean) * r * g + b) * (1 + sc) + sh  (layer)
+      // y = (x * r * g) * (1 + sc) + sh                (rms)
+      // in the reference's grouping, two lanes per instruction.
       uint32_t acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[r] = 0;
@@ -429,26 +435,26 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
           const float4 sh = lds16f(tsh + c);
           float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
           if constexpr (NORM == JO_NORM_LAYER) b = lds16f(tb + c);
+          const float2 g01 = make_float2(g.x, g.y), g23 = make_float2(g.z, g.w);
+          const float2 c01 = make_float2(sc.x, sc.y), c23 = make_float2(sc.z, sc.w);
+          const float2 s01 = make_float2(sh.x, sh.y), s23 = make_float2(sh.z, sh.w);
+          const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             uint32_t* wr = reinterpret_cast<uint32_t*>(&X[r][i].raw);
-            const float2 f0 = unpack2_r<T>(wr[2 * h]);
-            const float2 f1 = unpack2_r<T>(wr[2 * h + 1]);
-            const float m = mean[r], rv = rr[r];
-            float y0, y1, y2, y3;
+            const float2 rv = make_float2(rr[r], rr[r]);
+            float2 f0 = unpack2_r<T>(wr[2 * h]);
+            float2 f1 = unpack2_r<T>(wr[2 * h + 1]);
             if constexpr (NORM == JO_NORM_LAYER) {
-              y0 = ((f0.x - m) * rv * g.x + b.x) * sc.x + sh.x;
-              y1 = ((f0.y - m) * rv * g.y + b.y) * sc.y + sh.y;
-              y2 = ((f1.x - m) * rv * g.z + b.z) * sc.z + sh.z;
-              y3 = ((f1.y - m) * rv * g.w + b.w) * sc.w + sh.w;
+              const float2 nm = make_float2(-mean[r], -mean[r]);
+              f0 = fma2(fma2(mul2(add2(f0, nm), rv), g01, b01), c01, s01);
+              f1 = fma2(fma2(mul2(add2(f1, nm), rv), g23, b23), c23, s23);
             } else {
-              y0 = (f0.x * rv * g.x) * sc.x + sh.x;
-              y1 = (f0.y * rv * g.y) * sc.y + sh.y;
-              y2 = (f1.x * rv * g.z) * sc.z + sh.z;
-              y3 = (f1.y * rv * g.w) * sc.w + sh.w;
+              f0 = fma2(mul2(mul2(f0, rv), g01), c01, s01);
+              f1 = fma2(mul2(mul2(f1, rv), g23), c23, s23);
             }
-            wr[2 * h] = pack2<T>(y0, y1);      // RNE to T, as the reference's T(float) store
-            wr[2 * h + 1] = pack2<T>(y2, y3);
+            wr[2 * h] = pack2<T>(f0.x, f0.y);      // RNE to T, as the reference's T(float) store
+            wr[2 * h + 1] = pack2<T>(f1.x, f1.y);
             if constexpr (OP == OP_NORM_MOD_QUANT) {
               acc[r] = absmax2(acc[r], wr[2 * h]);
               acc[r] = absmax2(acc[r], wr[2 * h + 1]);

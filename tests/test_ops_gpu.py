@@ -217,9 +217,11 @@ def test_norm_modulate_quant(jo, cuda, M, N, groups, nt, affine):
     sh_t = T(sh) if groups > 1 else T(sh[0])
     jo.norm_modulate_quant_fp8(T(x), T(g), T(b), sc_t, sh_t, nt, 1e-6, q, s)
     # (1) quant half is bit-exact against quantising our own K2 output
-    sce = sc_t.repeat_interleave(M // groups, 0) if groups > 1 else sc_t.expand(M, N)
-    she = sh_t.repeat_interleave(M // groups, 0) if groups > 1 else sh_t.expand(M, N)
-    y = jo.fused_norm_scale_shift(T(x), T(g), T(b), sce.contiguous(), she.contiguous(), nt, 1e-6)
+    # Same kernel family as the fused call: broadcast view for one modulation
+    # row (staged kernel), per-row table otherwise (register kernel).
+    sce = sc_t.repeat_interleave(M // groups, 0).contiguous() if groups > 1 else sc_t.expand(M, N)
+    she = sh_t.repeat_interleave(M // groups, 0).contiguous() if groups > 1 else sh_t.expand(M, N)
+    y = jo.fused_norm_scale_shift(T(x), T(g), T(b), sce, she, nt, 1e-6)
     rq, rs = O.per_token_quant_fp8(to_np(y))
     assert np.array_equal(codes_np(q), rq)
     assert np.array_equal(s.cpu().numpy(), rs)

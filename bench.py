@@ -286,7 +286,7 @@ def run_ours(args):
             "gpu_launches": K,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": args.traffic,
-                         "peak_source": pk["source"], "kernel": "row_kernel<bf16,NORM_MOD_QUANT,RMS,64,16>",
+                         "peak_source": pk["source"], "kernel": "staged_rows<bf16,NORM_MOD_QUANT,RMS,4,2,2>",
                          "avg_launch_us": round(avg_launch_us, 3)},
             "clocks": clocks,
         }
@@ -559,11 +559,21 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip per-kernel table / CPU baseline")
     ap.add_argument("--no-stack", action="store_true", help="skip the 40-layer block-stack timing")
+    ap.add_argument("--only-stack", action="store_true", help="run only the block-stack timing (profiling aid)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per launch, if measured")
+    # DRAM bytes (read + write) of one launch of the headline kernel, measured with
+    # ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum on this workload:
+    # 107,897,344 read + 17,900,544 written (part of the 53.9 MB of codes is still
+    # in L2 when the kernel ends, so the write counter undercounts).
+    ap.add_argument("--traffic", type=float, default=107897344 + 17900544,
+                    help="DRAM bytes per launch of the headline kernel (ncu)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.only_stack:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps({"stack": stack_bench(torch, torch.device("cuda", 0), 1)}), flush=True)
     else:
         run_ours(args)
 

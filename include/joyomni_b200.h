@@ -41,6 +41,7 @@ extern "C" {
 /* ---- GEMM epilogues --------------------------------------------------- */
 #define JO_EPI_NONE 0
 #define JO_EPI_GELU_TANH 1
+#define JO_EPI_RESID_GATE 2   /* out = residual + gate[n] * out (jo_fp8_scaled_mm_ex) */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int jo_version(void);
@@ -138,6 +139,17 @@ int jo_norm_modulate_quant_fp8(const void* x, const void* gamma, const void* bet
 int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
                      const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
                      void* stream);
+
+/*
+ * Extended GEMM entry (no reference counterpart): jo_fp8_scaled_mm plus the
+ * gated-residual epilogue JO_EPI_RESID_GATE, out = out_dtype(residual[m, n] +
+ * gate[n] * out_dtype(GEMM result)) -- the model's torch.addcmul after the
+ * projection GEMMs (deploy/xvideo/models/dit/sgl_fused_ops.py:114-117) folded
+ * into the epilogue.  residual: [M, N] of out_dtype (may alias out); gate: [N].
+ */
+int jo_fp8_scaled_mm_ex(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                        const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
+                        const void* residual, const void* gate, void* stream);
 
 /* Diagnostic: fault code left by a GEMM wait that timed out (0 = none);
  * reset != 0 clears it.  Synchronous; for tests. */

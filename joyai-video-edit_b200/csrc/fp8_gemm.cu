@@ -152,7 +152,74 @@ struct Params {
   int M, N, K;
   int m_blocks, n_blocks, k_blocks;
   int epilogue;  // JO_EPI_*
+  const void* resid;  // JO_EPI_RESID_GATE: residual [M, N] (may alias d)
+  const void* gate;   // JO_EPI_RESID_GATE: gate [N]
 };
+
+// Epilogue of one 32-column chunk of one output row (one thread = one row):
+//   o = out(fma(sa, sb[n] * acc, bias[n]))  or  out(sa * (sb[n] * acc))
+//   GELU:        o = out(gelu_tanh(o))
+//   RESID_GATE:  o = out(res[m, n] + gate[n] * o)
+// (fp8_gemm.cu:833-860 of the reference for the first line; the GELU and
+// gated-residual forms are the model's following eager ops, dit.py:90-92 and
+// sgl_fused_ops.py:114-117, applied to the rounded GEMM output.)
+template <typename OutT>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Params& p, int m, float sa, int n0,
+                                               OutT* drow) {
+  const OutT* bias = static_cast<const OutT*>(p.bias);
+  const bool full = n0 + 32 <= p.N;
+  float y[32];
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    float sbv[4], bv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (full) {
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
+      sbv[0] = s4.x; sbv[1] = s4.y; sbv[2] = s4.z; sbv[3] = s4.w;
+      if (bias) {
+        const uint2 b2 = __ldg(reinterpret_cast<const uint2*>(bias + n0 + j));
+        const OutT* bb = reinterpret_cast<const OutT*>(&b2);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) bv[e] = to_f32(bb[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int n = n0 + j + e;
+        sbv[e] = n < p.N ? p.sb[n] : 0.f;
+        if (bias) bv[e] = n < p.N ? to_f32(bias[n]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float acc = __uint_as_float(r[j + e]);
+      const float tt = __fmul_rn(sbv[e], acc);
+      float o = bias ? __fmaf_rn(sa, tt, bv[e]) : __fmul_rn(sa, tt);
+      if (p.epilogue == JO_EPI_GELU_TANH) o = gelu_tanh(to_f32(from_f32<OutT>(o)));
+      y[j + e] = o;
+    }
+  }
+  if (p.epilogue == JO_EPI_RESID_GATE) {
+    const OutT* res = static_cast<const OutT*>(p.resid) + (size_t)m * p.N;
+    const OutT* gate = static_cast<const OutT*>(p.gate);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      if (full || n < p.N) y[j] = __fmaf_rn(to_f32(gate[n]), to_f32(from_f32<OutT>(y[j])), to_f32(res[n]));
+    }
+  }
+  if (full) {
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = pack2<OutT>(y[2 * j], y[2 * j + 1]);
+    uint4* dst = reinterpret_cast<uint4*>(drow + n0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.N) drow[n0 + j] = from_f32<OutT>(y[j]);
+  }
+}
 
 // Grouped rasterisation: GROUP m-blocks share the n sweep, keeping the live
 // A and B panels of all 148 CTAs inside L2.
@@ -281,7 +348,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row_in_tile = quarter * 32 + lane;
     int tc = 0;
     OutT* D = static_cast<OutT*>(p.d);
-    const OutT* bias = static_cast<const OutT*>(p.bias);
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
       int mb, nb;
       tile_coords(t, p, mb, nb);
@@ -302,49 +368,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_wait_ld();
         const int n0 = nb * BN + c;
         if (!mok || n0 >= p.N) continue;
-        float y[32];
-        const bool full = n0 + 32 <= p.N;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float sbv[4], bv[4] = {0.f, 0.f, 0.f, 0.f};
-          if (full) {
-            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
-            sbv[0] = s4.x; sbv[1] = s4.y; sbv[2] = s4.z; sbv[3] = s4.w;
-            if (bias) {
-              const uint2 b2 = __ldg(reinterpret_cast<const uint2*>(bias + n0 + j));
-              const OutT* bb = reinterpret_cast<const OutT*>(&b2);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) bv[e] = to_f32(bb[e]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int n = n0 + j + e;
-              sbv[e] = n < p.N ? p.sb[n] : 0.f;
-              if (bias) bv[e] = n < p.N ? to_f32(bias[n]) : 0.f;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float acc = __uint_as_float(r[j + e]);
-            const float tt = __fmul_rn(sbv[e], acc);
-            float o = bias ? __fmaf_rn(sa, tt, bv[e]) : __fmul_rn(sa, tt);
-            if (p.epilogue == JO_EPI_GELU_TANH) o = gelu_tanh(to_f32(from_f32<OutT>(o)));
-            y[j + e] = o;
-          }
-        }
-        if (full) {
-          uint32_t w[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = pack2<OutT>(y[2 * j], y[2 * j + 1]);
-          uint4* dst = reinterpret_cast<uint4*>(drow + n0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) drow[n0 + j] = from_f32<OutT>(y[j]);
-        }
+        epilogue_chunk<OutT>(r, p, m, sa, n0, drow);
       }
       // hand the accumulator back to the MMA warp
       fence_before();
@@ -572,7 +596,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t ltempty0 = map_to_rank(tempty0, 0);
     int tc = 0;
     OutT* D = static_cast<OutT*>(p.d);
-    const OutT* bias = static_cast<const OutT*>(p.bias);
     for (int t = pair; t < num_tiles; t += npairs, ++tc) {
       int mb, nb;
       tile_coords2(t, p.m_blocks, p.n_blocks, mb, nb);
@@ -593,49 +616,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         tmem_wait_ld();
         const int n0 = nb * BN + c;
         if (!mok || n0 >= p.N) continue;
-        float y[32];
-        const bool full = n0 + 32 <= p.N;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float sbv[4], bv[4] = {0.f, 0.f, 0.f, 0.f};
-          if (full) {
-            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + j));
-            sbv[0] = s4.x; sbv[1] = s4.y; sbv[2] = s4.z; sbv[3] = s4.w;
-            if (bias) {
-              const uint2 b2 = __ldg(reinterpret_cast<const uint2*>(bias + n0 + j));
-              const OutT* bb = reinterpret_cast<const OutT*>(&b2);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) bv[e] = to_f32(bb[e]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int n = n0 + j + e;
-              sbv[e] = n < p.N ? p.sb[n] : 0.f;
-              if (bias) bv[e] = n < p.N ? to_f32(bias[n]) : 0.f;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float acc = __uint_as_float(r[j + e]);
-            const float tt = __fmul_rn(sbv[e], acc);
-            float o = bias ? __fmaf_rn(sa, tt, bv[e]) : __fmul_rn(sa, tt);
-            if (p.epilogue == JO_EPI_GELU_TANH) o = gelu_tanh(to_f32(from_f32<OutT>(o)));
-            y[j + e] = o;
-          }
-        }
-        if (full) {
-          uint32_t w[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = pack2<OutT>(y[2 * j], y[2 * j + 1]);
-          uint4* dst = reinterpret_cast<uint4*>(drow + n0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) drow[n0 + j] = from_f32<OutT>(y[j]);
-        }
+        epilogue_chunk<OutT>(r, p, m, sa, n0, drow);
       }
       fence_before();
       __syncwarp();
@@ -731,7 +712,7 @@ int launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, Params p, cudaStrea
 
 template <typename OutT>
 int launch(const void* A, const void* B, const float* sa, const float* sb, const void* bias, void* D, int64_t M,
-           int64_t N, int64_t K, int epi, cudaStream_t st) {
+           int64_t N, int64_t K, int epi, const void* resid, const void* gate, cudaStream_t st) {
   CUtensorMap ta, tb;
   const bool pair = M > 128 && use_2sm();
   if (!make_map(&ta, A, M, K, BM) || !make_map(&tb, B, N, K, pair ? 128 : BN)) {
@@ -751,6 +732,8 @@ int launch(const void* A, const void* B, const float* sa, const float* sb, const
   p.n_blocks = (int)((N + BN - 1) / BN);
   p.k_blocks = (int)((K + BK - 1) / BK);
   p.epilogue = epi;
+  p.resid = resid;
+  p.gate = gate;
   if (pair) return launch_2sm<OutT>(ta, tb, p, st);
   const int smem = STAGES * STAGE_BYTES + 1024 + 256;
   static bool attr = false;
@@ -769,15 +752,17 @@ int launch(const void* A, const void* B, const float* sa, const float* sb, const
 
 extern "C" {
 
-int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
-                     const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
-                     void* stream) {
+int jo_fp8_scaled_mm_ex(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                        const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
+                        const void* residual, const void* gate, void* stream) {
   using namespace jo;
   const char* what = "fp8_scaled_mm";
   JO_REQUIRE(out_dtype == JO_DTYPE_BF16 || out_dtype == JO_DTYPE_F16, JO_ERR_DTYPE,
              "out_dtype must be Half or BFloat16");
-  JO_REQUIRE(epilogue == JO_EPI_NONE || epilogue == JO_EPI_GELU_TANH, JO_ERR_INVALID, "%s: unknown epilogue %d",
-             what, epilogue);
+  JO_REQUIRE(epilogue == JO_EPI_NONE || epilogue == JO_EPI_GELU_TANH || epilogue == JO_EPI_RESID_GATE,
+             JO_ERR_INVALID, "%s: unknown epilogue %d", what, epilogue);
+  JO_REQUIRE(epilogue != JO_EPI_RESID_GATE || (residual && gate), JO_ERR_INVALID,
+             "%s: the gated-residual epilogue needs residual and gate", what);
   JO_REQUIRE(M >= 0 && N >= 0 && K >= 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), JO_ERR_INVALID,
              "%s: invalid shape", what);
   JO_REQUIRE(K % 16 == 0, JO_ERR_INVALID, "mat_a must be multiple of 16 bytes for memory alignment");
@@ -790,11 +775,24 @@ int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a
   int st = require_sm100();
   if (st != JO_OK) return st;
   if (M == 0 || N == 0) return JO_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   JO_REQUIRE(K > 0, JO_ERR_INVALID, "%s: K must be positive", what);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   return out_dtype == JO_DTYPE_BF16
-             ? gemm::launch<__nv_bfloat16>(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, epilogue, s)
-             : gemm::launch<__half>(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, epilogue, s);
+             ? gemm::launch<__nv_bfloat16>(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, epilogue, residual,
+                                           gate, s)
+             : gemm::launch<__half>(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, epilogue, residual, gate,
+                                    s);
+}
+
+int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                     const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
+                     void* stream) {
+  if (epilogue == JO_EPI_RESID_GATE) {
+    jo::set_error("fp8_scaled_mm: the gated-residual epilogue needs jo_fp8_scaled_mm_ex");
+    return JO_ERR_INVALID;
+  }
+  return jo_fp8_scaled_mm_ex(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, out_dtype, epilogue, nullptr,
+                             nullptr, stream);
 }
 
 // Fault code of the GEMM kernel's bounded waits (0 = none) and reset.  Reads

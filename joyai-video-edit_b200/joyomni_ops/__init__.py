@@ -34,6 +34,7 @@ __all__ = [
     "norm_modulate_quant_fp8",
     "fp8_scaled_mm_gelu",
     "qk_norm_rope_strided",
+    "fp8_scaled_mm_residual",
 ]
 
 _DT = {torch.float32: _lib.JO_DTYPE_F32, torch.float16: _lib.JO_DTYPE_F16, torch.bfloat16: _lib.JO_DTYPE_BF16}
@@ -316,33 +317,54 @@ def _fp8_mm_checks(mat_a, mat_b, scales_a, scales_b, out_dtype, bias):
          "out must be multiple of 16 bytes for memory alignment")
 
 
-def _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, epilogue):
+def _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, epilogue, out=None, residual=None, gate=None):
     if not has_fp8():
         raise NotImplementedError("joyomni_b200 was built without the FP8 GEMM")
     _fp8_mm_checks(mat_a, mat_b, scales_a, scales_b, out_dtype, bias)
     M, K = mat_a.shape
     N = mat_b.size(1)
-    out = torch.empty((M, N), dtype=out_dtype, device=mat_a.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=mat_a.device)
+    else:
+        _chk(out.shape == (M, N) and out.dtype == out_dtype and out.is_cuda, "out must be [M, N] of out_dtype")
+        _chk(out.stride(1) == 1 and (M <= 1 or out.stride(0) == N), "out rows must be dense")
+    if residual is not None:
+        _chk(residual.shape == (M, N) and residual.dtype == out_dtype and residual.stride(1) == 1
+             and (M <= 1 or residual.stride(0) == N), "residual must be a dense [M, N] tensor of out_dtype")
+        _chk(gate is not None and gate.numel() == N and gate.dtype == out_dtype, "gate must be [N] of out_dtype")
+        gate = gate.contiguous()
     lda = mat_a.stride(0) if M > 1 else K
     ldb = mat_b.stride(1) if N > 1 else K
     _chk(lda == K and ldb == K, "mat_a rows and mat_b columns must be densely packed")
     with _Device(mat_a) as st:
-        _check(_L.jo_fp8_scaled_mm(
+        _check(_L.jo_fp8_scaled_mm_ex(
             mat_a.data_ptr(), mat_b.data_ptr(), scales_a.data_ptr(), scales_b.data_ptr(),
             bias.data_ptr() if bias is not None else None, out.data_ptr(), M, N, K,
-            _DT[out_dtype], epilogue, st))
+            _DT[out_dtype], epilogue, residual.data_ptr() if residual is not None else None,
+            gate.data_ptr() if gate is not None else None, st))
     return out
 
 
-def fp8_scaled_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias: Optional[torch.Tensor] = None):
-    return _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, _lib.JO_EPI_NONE)
+def fp8_scaled_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias: Optional[torch.Tensor] = None, *, out=None):
+    """Reference signature; `out` (keyword, an extension) writes into a caller
+    buffer, e.g. a row slice of a larger [L, N] tensor."""
+    return _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, _lib.JO_EPI_NONE, out=out)
 
 
-def fp8_scaled_mm_gelu(mat_a, mat_b, scales_a, scales_b, out_dtype, bias: Optional[torch.Tensor] = None):
+def fp8_scaled_mm_gelu(mat_a, mat_b, scales_a, scales_b, out_dtype, bias: Optional[torch.Tensor] = None, *,
+                       out=None):
     """gelu_tanh(fp8_scaled_mm(...)): GELU applied to the rounded GEMM output, as the
     reference model applies F.gelu(approximate="tanh") after fp8_scaled_mm
     (deploy/xvideo/models/dit/dit.py:90-92)."""
-    return _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, _lib.JO_EPI_GELU_TANH)
+    return _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, _lib.JO_EPI_GELU_TANH, out=out)
+
+
+def fp8_scaled_mm_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, residual, gate, *, out=None):
+    """residual + gate * fp8_scaled_mm(...) (rounded GEMM output, then the gated
+    add of torch.addcmul(residual, y, gate), deploy/xvideo/models/dit/sgl_fused_ops.py:114-117)
+    in the GEMM epilogue.  out may be the residual itself (in place)."""
+    return _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, _lib.JO_EPI_RESID_GATE, out=out,
+                   residual=residual, gate=gate)
 
 
 from . import _torch_ops  # noqa: E402,F401  (registers torch.ops.joyomni_ops.*)

@@ -35,6 +35,7 @@ JO_NORM_RMS = 1
 
 JO_EPI_NONE = 0
 JO_EPI_GELU_TANH = 1
+JO_EPI_RESID_GATE = 2
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -53,6 +54,7 @@ SIGNATURES = {
     "jo_per_token_quant_fp8": [_p, _i32, _p, _p, _i64, _i64, _p],
     "jo_norm_modulate_quant_fp8": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _p, _p, _p],
     "jo_fp8_scaled_mm": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
+    "jo_fp8_scaled_mm_ex": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p, _p, _p],
     "jo_gemm_last_fault": [_i32],
 }
 

@@ -11,8 +11,9 @@ random-initialised weights and synthetic inputs.  Per block and stream:
   q, k = RMSNorm_head + 3D RoPE, in place in the qkv buffer (image stream);     (dit.py:364-370)
          RMSNorm_head only (text stream)                                        (dit.py:384-385)
   attn = SDPA(q_img|q_txt, [k_cache | k_img | k_txt], [v ...])                   (dit.py:387-420)
-  x    = x + gate1 * fp8_linear(attn, W_proj)                                   (dit.py:463-466)
+  x    = x + gate1 * fp8_linear(attn, W_proj)     residual in the GEMM epilogue  (dit.py:463-466)
   x    = x + gate2 * fp8_linear(gelu_tanh(fp8_linear(mod2(LN(x)), W_up)), W_down)  (dit.py:467-476)
+         (GELU in the up-projection epilogue, gated residual in the down-projection epilogue)
 
 Differences from the reference model that the synthetic configuration asks
 for or that are harness simplifications: BASELINE's dims (hidden 5120, 40
@@ -91,9 +92,13 @@ class Fp8Weight:
     def t(self):  # column-major [K, N] view, as fp8_scaled_mm wants
         return self.codes.t()
 
-    def __call__(self, xq, xs, gelu=False):
+    def __call__(self, xq, xs, gelu=False, out=None):
         f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
-        return f(xq, self.t, xs, self.scale, torch.bfloat16, self.b)
+        return f(xq, self.t, xs, self.scale, torch.bfloat16, self.b, out=out)
+
+    def residual(self, xq, xs, res, gate, out=None):
+        """res + gate * (x @ W + b), gated residual fused in the GEMM epilogue."""
+        return jo.fp8_scaled_mm_residual(xq, self.t, xs, self.scale, torch.bfloat16, self.b, res, gate, out=out)
 
 
 def quant(x):
@@ -176,21 +181,20 @@ class Block:
         im = (self.img.mod + vec).unbind(0)
         tm = (self.txt.mod + vec).unbind(0)
 
-        # ---- QKV, per stream, on this rank's tokens -----------------------
+        # ---- QKV of both streams into one [L_local, 3, H, Dh] buffer --------
+        qkv = torch.empty((Li + Lt, 3 * D), dtype=torch.bfloat16, device=img.device)
         xq, xs = norm_mod_quant(img, im[0], im[1])
-        iqkv = self.img.qkv(xq, xs).view(1, Li, 3, H, Dh)
-        jo.qk_norm_rope_strided(iqkv[:, :, 0], iqkv[:, :, 1], NORM_EPS, self.img.q_norm, self.img.k_norm, cos, sin)
+        self.img.qkv(xq, xs, out=qkv[:Li])
         tq, ts = norm_mod_quant(txt, tm[0], tm[1])
-        tqkv = self.txt.qkv(tq, ts).view(1, Lt, 3, H, Dh)
-        jo.qk_norm_rope_strided(tqkv[:, :, 0], tqkv[:, :, 1], NORM_EPS, self.txt.q_norm, self.txt.k_norm)
+        self.txt.qkv(tq, ts, out=qkv[Li:])
+        v5 = qkv.view(1, Li + Lt, 3, H, Dh)
+        jo.qk_norm_rope_strided(v5[:, :Li, 0], v5[:, :Li, 1], NORM_EPS, self.img.q_norm, self.img.k_norm, cos, sin)
+        jo.qk_norm_rope_strided(v5[:, Li:, 0], v5[:, Li:, 1], NORM_EPS, self.txt.q_norm, self.txt.k_norm)
 
         # ---- attention over [current | cached] keys, head-sharded ------------
-        def cat_seq(i):
-            return torch.cat((iqkv[0, :, i], tqkv[0, :, i]), 0)             # [L_local, H, Dh]
-
-        q = sp.seq_to_heads(cat_seq(0))
-        sp.seq_to_heads(cat_seq(1), out=kv.k[:kv.cur])
-        sp.seq_to_heads(cat_seq(2), out=kv.v[:kv.cur])
+        q = v5[0, :, 0] if sp.world == 1 else sp.seq_to_heads(v5[0, :, 0])     # strided view when P = 1
+        sp.seq_to_heads(v5[0, :, 1], out=kv.k[:kv.cur])
+        sp.seq_to_heads(v5[0, :, 2], out=kv.v[:kv.cur])
         k_all, v_all = kv.keys()
         with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
                                              torch.nn.attention.SDPBackend.FLASH_ATTENTION,
@@ -207,11 +211,11 @@ class Block:
     @staticmethod
     def _tail(st: Stream, m, x, attn):
         aq, as_ = quant(attn)
-        x = torch.addcmul(x, st.proj(aq, as_), m[2])
+        x = st.proj.residual(aq, as_, x, m[2])                      # x + gate1 * proj(attn)
         hq, hs = norm_mod_quant(x, m[3], m[4])
         h = st.up(hq, hs, gelu=True)
         h2q, h2s = quant(h)
-        return torch.addcmul(x, st.down(h2q, h2s), m[5])
+        return st.down.residual(h2q, h2s, x, m[5], out=x)            # x + gate2 * down(h), in place
 
 
 class Stack:

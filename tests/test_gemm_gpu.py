@@ -103,3 +103,38 @@ def test_fp8_scaled_mm_full_size_row_sample(jo, cuda, N, gelu):
     ref = O.fp8_scaled_mm(a[rows], b, sa[rows], sb, bias, epilogue="gelu_tanh" if gelu else "none")
     assert_close_ulp(y[rows], ref, max_ulp=2, rel_rms=2e-3 if gelu else 1e-3, atol=1e-4 if gelu else 1e-6)
     assert np.isfinite(y).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 256, 512), (77, 264, 128), (1000, 768, 640)])
+def test_fp8_scaled_mm_residual_epilogue(jo, cuda, M, N, K):
+    """out = residual + gate * bf16(GEMM): the model's addcmul after the projection
+    GEMMs, fused; in place on the residual as the block uses it."""
+    rng = np.random.default_rng(M + N)
+    a, sa, b, sb = _operands(rng, M, N, K)
+    bias = randn(rng, (N,), 0.01)
+    res = randn(rng, (M, N), 1.0)
+    gate = randn(rng, (N,), 0.5)
+    A = torch.from_numpy(a).to(cuda).view(torch.float8_e4m3fn)
+    B = torch.from_numpy(b).to(cuda).view(torch.float8_e4m3fn).t()
+    rt = torch.from_numpy(res).to(torch.bfloat16).to(cuda)
+    gt = torch.from_numpy(gate).to(torch.bfloat16).to(cuda)
+    plain = jo.fp8_scaled_mm(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), torch.bfloat16,
+                             torch.from_numpy(bias).to(torch.bfloat16).to(cuda))
+    expect = torch.addcmul(rt, plain, gt)
+    y = jo.fp8_scaled_mm_residual(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda),
+                                  torch.bfloat16, torch.from_numpy(bias).to(torch.bfloat16).to(cuda), rt, gt, out=rt)
+    assert y.data_ptr() == rt.data_ptr()
+    assert_close_ulp(y.float().cpu().numpy(), expect.float().cpu().numpy(), max_ulp=1, rel_rms=1e-3)
+
+
+def test_fp8_scaled_mm_out_row_slice(jo, cuda):
+    rng = np.random.default_rng(8)
+    a, sa, b, sb = _operands(rng, 200, 256, 256)
+    A = torch.from_numpy(a).to(cuda).view(torch.float8_e4m3fn)
+    B = torch.from_numpy(b).to(cuda).view(torch.float8_e4m3fn).t()
+    big = torch.full((300, 256), 7.0, dtype=torch.bfloat16, device=cuda)
+    ref = jo.fp8_scaled_mm(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), torch.bfloat16)
+    jo.fp8_scaled_mm(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), torch.bfloat16,
+                     out=big[50:250])
+    assert torch.equal(big[50:250], ref)
+    assert (big[:50] == 7).all() and (big[250:] == 7).all()

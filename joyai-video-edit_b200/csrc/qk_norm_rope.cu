@@ -5,10 +5,9 @@
 // Design (B200): one head vector (D bf16) is owned by D/8 lanes that each move
 // one 16-byte vector, so a warp covers 32*8/D heads and every access is a full
 // 16-byte coalesced load/store.  The same lanes process the q and the k vector
-// of a (token, head) slot, so the per-lane norm weights live in registers for
-// the whole kernel and the token's cos/sin entries are fetched once (L1) for
-// both.  Each warp handles U slot groups with all loads issued before any math
-// (2*U 16-byte loads in flight per lane) to keep HBM busy.
+// of a (token, head) slot, so the per-lane norm weights live in registers and
+// the token's cos/sin entries are fetched once (L1) for both.  Each warp
+// handles U slot groups with all loads issued before any math.
 //
 // Numerics: the sum of squares is accumulated and reduced in exactly the
 // reference's order.  The reference gives each of 32 lanes D/32 consecutive
@@ -19,6 +18,8 @@
 // reference sum bit for bit.  Scaling, weighting and rotation use the
 // reference's expression forms (x * (r * w); x1*c - x2*s; x1*s + x2*c).
 #include "jo_common.cuh"
+
+#include <stdlib.h>
 
 namespace jo {
 namespace {
@@ -122,10 +123,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   }
 }
 
-template <int D>
-int launch(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
-           const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
-  constexpr int U = 2;
+template <int D, int U>
+int launch_u(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
+             const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
   constexpr int HPW = 32 / (D / 8);
   const int64_t warps = (slots + (int64_t)HPW * U - 1) / ((int64_t)HPW * U);
   const int64_t blocks = (warps + 7) / 8;
@@ -142,6 +142,31 @@ int launch(void* q, void* k, int64_t slots, int seq_len, int num_heads, float ep
     qk_norm_rope_kernel<D, U, false><<<(unsigned)blocks, 256, 0, st>>>(qp, kp, slots, seq_len, num_heads, eps, qwp,
                                                                        kwp, cp, sp, q_ts, k_ts);
   return check_launch("fused_qk_norm_rope_3d_paired");
+}
+
+// Slot groups per warp (loads in flight per lane = 2 * U).  U = 1 measured
+// fastest on B200 (more CTAs in flight beat deeper per-warp batches);
+// JO_QKR_U overrides for measurements.
+static int qkr_u() {
+  static int u = -1;
+  if (u < 0) {
+    const char* e = getenv("JO_QKR_U");
+    u = e ? atoi(e) : 1;
+    if (u != 1 && u != 2 && u != 4 && u != 8) u = 1;
+  }
+  return u;
+}
+
+template <int D>
+int launch(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
+           const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
+  switch (qkr_u()) {
+    case 1: return launch_u<D, 1>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+    case 4: return launch_u<D, 4>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+    case 8: return launch_u<D, 8>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+    case 2: return launch_u<D, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+    default: return launch_u<D, 1>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  }
 }
 
 }  // namespace

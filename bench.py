@@ -19,8 +19,9 @@ Multi-GPU (torchrun): every rank runs the same per-rank workload on its own
 rows (the ops are independent per token; no collective on the data path),
 "scaling": "weak"; time = max over ranks; value = total bytes / that time.
 
---impl reference: the reference's CPU path (the oracle restatement of its
-kernels, numpy, all host threads) on a bounded row sample of the same workload.
+--impl reference: the reference's CPU path (its eager-torch formulas, restated
+in oracle/torch_eager.py, all host threads) on a bounded row sample of the same
+workload.
 """
 from __future__ import annotations
 
@@ -475,51 +476,40 @@ def reference_gpu_table():
 
 # ------------------------------------------------------- CPU baselines -----
 def _cpu_sample(rows, seed=2):
-    import numpy as np
-
-    import joyomni_oracle as O
-    rng = np.random.default_rng(seed)
-    x = rng.standard_normal((rows, N_CFG2)).astype(np.float32)
-    x[rng.random((rows, N_CFG2)) < 0.01] *= np.float32(50.0)
-    x = O.round_bf16(x)
-    w = O.round_bf16(1 + 0.1 * rng.standard_normal(N_CFG2).astype(np.float32))
-    sh = O.round_bf16(0.1 * rng.standard_normal(N_CFG2).astype(np.float32))
-    sc = O.round_bf16(0.1 * rng.standard_normal(N_CFG2).astype(np.float32))
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x, w, sh, sc = make_cfg2_inputs(torch, "cpu", seed, M=rows)
     return x, w, sh, sc
 
 
 def _cpu_step(x, w, sh, sc, threads):
-    import numpy as np
+    import torch
 
-    import joyomni_oracle as O
-
-    def work(lo, hi):
-        y = O.fused_norm_scale_shift(x[lo:hi], w, None, sc, sh, 1, 1e-6)
-        return O.per_token_quant_fp8(y)
-
-    if threads <= 1:
-        return work(0, x.shape[0])
-    from concurrent.futures import ThreadPoolExecutor
-    chunks = np.linspace(0, x.shape[0], threads + 1).astype(int)
-    with ThreadPoolExecutor(threads) as ex:
-        return list(ex.map(lambda i: work(chunks[i], chunks[i + 1]), range(threads)))
+    import torch_eager
+    torch.set_num_threads(threads)
+    return torch_eager.cfg2_chain(x, w, sh, sc)
 
 
 def cpu_baseline(seconds):
-    """Oracle (numpy port of the reference kernels) on a bounded row sample."""
-    rows = 64
+    """The reference's eager-torch path for config 2 (oracle/torch_eager.py) on a
+    bounded row sample, on all host cores."""
+    threads = os.cpu_count() or 1
+    rows = 256
     x, w, sh, sc = _cpu_sample(rows)
+    _cpu_step(x, w, sh, sc, threads)
     t0 = time.perf_counter()
-    _cpu_step(x, w, sh, sc, 1)
+    _cpu_step(x, w, sh, sc, threads)
     dt = time.perf_counter() - t0
-    rows = int(max(64, min(M_CFG2, rows * seconds / max(dt, 1e-3))))
+    rows = int(max(256, min(M_CFG2, rows * seconds / max(dt, 1e-3))))
     x, w, sh, sc = _cpu_sample(rows)
+    _cpu_step(x, w, sh, sc, threads)
     t0 = time.perf_counter()
-    _cpu_step(x, w, sh, sc, 1)
+    _cpu_step(x, w, sh, sc, threads)
     dt = time.perf_counter() - t0
     gbs = cfg2_bytes(rows, N_CFG2) / dt / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{rows} of {M_CFG2} rows of cfg2 (fused RMSNorm+modulate+quant), numpy oracle, {dt:.1f} s"}
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {M_CFG2} rows of cfg2, eager-torch fp32 restatement of the reference "
+                      f"(norm_scale_shift RMS then per-token quant), {threads} threads, {dt:.2f} s"}
 
 
 def run_reference(args):
@@ -528,7 +518,7 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    rows = 1024
+    rows = 4096
     x, w, sh, sc = _cpu_sample(rows)
     for _ in range(max(args.warmup, 1)):
         _cpu_step(x, w, sh, sc, threads)
@@ -545,8 +535,8 @@ def run_reference(args):
             "config": {"workload": "cfg2: RMSNorm + adaLN modulate + per-token FP8 quant", "M": M_CFG2,
                        "N": N_CFG2, "sample_rows_per_step": rows},
             "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"{rows} rows of cfg2 per step, numpy oracle of the reference kernels "
-                                       f"(norm_scale_shift then per_token_quant), {threads} threads"},
+                             "sample": f"{rows} rows of cfg2 per step, eager-torch fp32 restatement of the "
+                                       f"reference (norm_scale_shift RMS then per-token quant), {threads} threads"},
             "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

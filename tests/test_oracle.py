@@ -214,3 +214,20 @@ GOLDEN_FILES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
 def test_oracle_against_reference_golden(path):
     import golden_cases
     golden_cases.check_oracle(path)
+
+
+def test_torch_eager_cpu_path_agrees_with_oracle():
+    """The eager-torch CPU baseline (oracle/torch_eager.py) computes the same
+    config-2 chain as the oracle: scales to fp32 rounding, codes almost all equal."""
+    import torch_eager
+    rng = np.random.default_rng(12)
+    M, N = 64, 1024
+    x = randn(rng, (M, N))
+    w = O.round_bf16(1 + 0.1 * rng.standard_normal(N).astype(np.float32))
+    sh, sc = randn(rng, (N,), 0.1), randn(rng, (N,), 0.1)
+    T = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    q, s = torch_eager.cfg2_chain(T(x), T(w), T(sh), T(sc))
+    y = O.fused_norm_scale_shift(x, w, None, sc, sh, 1, 1e-6)
+    oq, os_ = O.per_token_quant_fp8(y)
+    assert np.allclose(s.view(-1).numpy(), os_, rtol=1e-5)
+    assert (q.view(torch.uint8).numpy() != oq).mean() < 2e-3

@@ -310,7 +310,9 @@ def stack_bench(torch, dev, world):
     (hidden 5120, 40 heads, FFN 13824, 10530 image + 512 text tokens, KV cache of
     2 previous chunks pre-filled with N(0,1)), Ulysses over all ranks.  Times one
     block forward (config 4 at N = 1) and one chunk = 3 denoising steps x 40
-    layers + KV commit (config 5) after one warm chunk; max over ranks."""
+    layers + KV commit (config 5) after one warm chunk, eagerly and with each
+    40-layer step replayed from one CUDA graph (NCCL all-to-alls included);
+    max over ranks."""
     import torch.distributed as dist
     from joyomni_stack import Stack, StackConfig
     cfg = StackConfig()
@@ -347,12 +349,17 @@ def stack_bench(torch, dev, world):
 
     def chunk():
         state["x"] = st.denoise_chunk(state["x"], txt)
-    chunk_ms = timed(chunk, 1)
+    chunk_ms_eager = timed(chunk, 1)
+    graph = st.capture(txt)                           # whole 40-layer step in one CUDA graph
+    chunk()
+    chunk_ms = timed(chunk, 1) if graph else chunk_ms_eager
     finite = bool(torch.isfinite(state["x"]).all())
     gflop_block = 2 * (cfg.img_tokens + cfg.txt_tokens) * cfg.hidden * (4 * cfg.hidden + 2 * cfg.ffn) / 1e9
     attn_flop = 4 * (cfg.img_tokens + cfg.txt_tokens) * (cfg.img_tokens * 3 + cfg.txt_tokens) * cfg.hidden / 1e9
     out = {"config": "cfg4 block / cfg5 40 layers x 3 steps, 10530 img + 512 txt tokens, KV 2 chunks (post-RoPE)",
            "ulysses_degree": world, "block_ms": round(block_ms, 2), "chunk_ms": round(chunk_ms, 1),
+           "chunk_ms_eager": round(chunk_ms_eager, 1), "step_cuda_graph": graph,
+           **({} if graph else {"capture_error": getattr(st, "capture_error", "")}),
            "fps": round(24 / (chunk_ms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
            "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
            "attention": "torch SDPA (cuDNN/flash), bf16"}

@@ -142,7 +142,11 @@ template <> __device__ __forceinline__ float from_bits16<__half>(uint32_t b) {
 }
 // Running max of |elements| over packed pairs, on the integer bit patterns
 // (for non-NaN values |x| orders like its bits; NaN patterns sort above inf).
-__device__ __forceinline__ uint32_t absmax2(uint32_t acc, uint32_t w) { return __vmaxu2(acc, w & 0x7fff7fffu); }
+__device__ __forceinline__ uint32_t absmax2(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w & 0x7fff7fffu));
+  return r;
+}
 __device__ __forceinline__ uint32_t absmax2_fold(uint32_t acc) { return max(acc & 0xffffu, acc >> 16); }
 
 // ---- paired fp32 arithmetic (sm_100: one instruction, two IEEE RN lanes) ----
@@ -169,6 +173,18 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
       " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
       : "=f"(r.x), "=f"(r.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+// Four floats -> four e4m3 codes in one 32-bit word (element 0 in the low
+// byte), round-to-nearest-even, satfinite; the two 16-bit conversion results
+// are joined inside the asm block.
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  uint32_t r;
+  asm("{\n .reg .b16 lo, hi;\n cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
+      " mov.b32 %0, {lo, hi};\n}"
+      : "=r"(r)
+      : "f"(a), "f"(b), "f"(c), "f"(d));
   return r;
 }
 

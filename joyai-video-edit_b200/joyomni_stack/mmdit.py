@@ -258,12 +258,60 @@ class Stack:
         g = torch.Generator(device="cpu").manual_seed(int(t) * 7919 + 1)
         return torch.randn(self.cfg.hidden, generator=g).to(torch.bfloat16).to(self.device)
 
+    # ---- whole-step CUDA graph ---------------------------------------------
+    def capture(self, txt: torch.Tensor) -> bool:
+        """Capture one 40-layer forward (all joyomni_ops kernels, attention and, with
+        P > 1, the NCCL all-to-alls) into a CUDA graph over static input buffers
+        (the reference captures its denoise steps the same way,
+        deploy/xvideo/serving/graph_runner.py:97-183).  Every kernel here launches on
+        the current stream and allocates nothing itself, so the step is
+        capturable; returns False (eager execution stays in use) if capture fails."""
+        D = self.cfg.hidden
+        a, b = self.sp.img_range
+        dev = self.device
+        self._gx = torch.zeros((b - a, D), dtype=torch.bfloat16, device=dev)
+        self._gtxt = txt.clone()
+        self._gvec = torch.zeros(D, dtype=torch.bfloat16, device=dev)
+        saved = [(kv.valid, kv.next_slot) for kv in self.kv]
+        try:
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                for _ in range(2):
+                    self.forward(self._gx, self._gtxt, self._gvec)
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._gout, _ = self.forward(self._gx, self._gtxt, self._gvec)
+            self._graph = g
+            ok = True
+        except Exception as e:  # noqa: BLE001
+            self._graph = None
+            self.capture_error = repr(e)[:300]
+            ok = False
+        for kv, (v, n) in zip(self.kv, saved):
+            kv.valid, kv.next_slot = v, n
+        return ok
+
+    def _step(self, xb: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor):
+        g = getattr(self, "_graph", None)
+        if g is None:
+            return self.forward(xb, txt, vec)[0]
+        self._gx.copy_(xb)
+        self._gvec.copy_(vec)
+        if txt.data_ptr() != self._gtxt.data_ptr():
+            self._gtxt.copy_(txt)
+        g.replay()
+        return self._gout
+
     def denoise_chunk(self, x: torch.Tensor, txt: torch.Tensor, timesteps=(1000, 750, 500)):
         """3 denoising steps (Euler in fp32 over sigmas t/1000 -> next, last -> 0);
-        the chunk's image K/V from the last step enter the cache afterwards."""
+        the chunk's image K/V from the last step enter the cache afterwards.  Uses
+        the captured step graph when capture() succeeded."""
         sig = [t / 1000.0 for t in timesteps] + [0.0]
         for i, t in enumerate(timesteps):
-            v, _ = self.forward(x.to(torch.bfloat16), txt, self.timestep_vec(t))
+            v = self._step(x.to(torch.bfloat16), txt, self.timestep_vec(t))
             x = x + (sig[i + 1] - sig[i]) * v.float()
         self.commit_kv()
         return x

@@ -72,3 +72,22 @@ def test_ulysses_two_gpus_matches_one(cuda):
                        capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "ULYSSES_OK" in r.stdout, r.stdout[-2000:]
+
+
+def test_step_graph_matches_eager(cuda):
+    """A chunk replayed from the captured step graph equals eager execution."""
+    from joyomni_stack import Stack
+    cfg = _small_cfg(layers=2)
+    outs = []
+    for use_graph in (False, True):
+        st = Stack(cfg, cuda)
+        gen = torch.Generator(device=cuda).manual_seed(3)
+        for kv in st.kv:
+            kv.fill_random(gen, 2)
+        x, txt = st.inputs(4)
+        if use_graph:
+            assert st.capture(txt), getattr(st, "capture_error", "")
+        x = st.denoise_chunk(x, txt)
+        x = st.denoise_chunk(x, txt)
+        outs.append(x)
+    assert _rel(outs[1], outs[0]) < 1e-6

@@ -154,6 +154,7 @@ struct Params {
   int epilogue;  // JO_EPI_*
   const void* resid;  // JO_EPI_RESID_GATE: residual [M, N] (may alias d)
   const void* gate;   // JO_EPI_RESID_GATE: gate [N]
+  int group;          // 2-SM kernel: pair-tile rows per rasterisation group
 };
 
 // Epilogue of one 32-column chunk of one output row (one thread = one row):
@@ -466,8 +467,8 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
       : "memory");
 }
 
-__device__ __forceinline__ void tile_coords2(int t, int m_blocks, int n_blocks, int& mb, int& nb) {
-  constexpr int GROUP = 8;
+__device__ __forceinline__ void tile_coords2(int t, int m_blocks, int n_blocks, int group, int& mb, int& nb) {
+  const int GROUP = group;
   const int per_group = GROUP * n_blocks;
   const int g = t / per_group;
   const int first = g * GROUP;
@@ -535,7 +536,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         int mb, nb;
-        tile_coords2(t, p.m_blocks, p.n_blocks, mb, nb);
+        tile_coords2(t, p.m_blocks, p.n_blocks, p.group, mb, nb);
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1;
@@ -598,7 +599,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     OutT* D = static_cast<OutT*>(p.d);
     for (int t = pair; t < num_tiles; t += npairs, ++tc) {
       int mb, nb;
-      tile_coords2(t, p.m_blocks, p.n_blocks, mb, nb);
+      tile_coords2(t, p.m_blocks, p.n_blocks, p.group, mb, nb);
       const int buf = tc & 1;
       const uint32_t tph = (tc >> 1) & 1;
       if (!mbar_wait_cluster(tfull0 + 8 * buf, tph, abort_flag, 14)) break;
@@ -702,6 +703,19 @@ int launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, Params p, cudaStrea
     attr = true;
   }
   p.m_blocks = (p.M + 255) / 256;
+  static int group_env = -1;
+  if (group_env < 0) {
+    const char* e = getenv("JOYOMNI_GEMM_GROUP");
+    group_env = e ? atoi(e) : 0;
+  }
+  // Rasterisation: GROUP pair-tile rows (A panel of GROUP*256 rows) share each
+  // sweep over N.  ~28 MB of A per group keeps both the A panel and the B
+  // panels being swept resident in L2 (measured at M = 10530, K = 5120: group
+  // 21 reads 219 MB from DRAM against 515 MB for group 8, and runs 4 % faster
+  // under the power cap).
+  p.group = group_env > 0 ? group_env : (int)((28LL << 20) / (256LL * p.K));
+  if (p.group < 4) p.group = 4;
+  if (p.group > p.m_blocks) p.group = p.m_blocks;
   const int tiles = p.m_blocks * p.n_blocks;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   if (getenv("JOYOMNI_GEMM_DEBUG"))

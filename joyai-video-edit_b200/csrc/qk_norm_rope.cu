@@ -45,13 +45,19 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 
   Vec16<__nv_bfloat16> vq[U], vk[U];
   int64_t slot[U], qo[U], ko[U];
+  uint32_t tokr[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     slot[u] = (warp * U + u) * HPW + lane / LPH;
-    const int64_t tok = slot[u] / num_heads;          // (batch, token) row
-    const int64_t head = slot[u] - tok * num_heads;
-    qo[u] = tok * q_ts + head * D + hl * 8;
-    ko[u] = tok * k_ts + head * D + hl * 8;
+    // (batch, token) row and head of the slot; the host guarantees
+    // slots < 2^31, so 32-bit division suffices (64-bit division would cost
+    // ~10 instructions per element here).
+    const uint32_t s32 = (uint32_t)slot[u];
+    const uint32_t tok = s32 / (uint32_t)num_heads;
+    const uint32_t head = s32 - tok * (uint32_t)num_heads;
+    tokr[u] = tok;
+    qo[u] = (int64_t)tok * q_ts + head * D + hl * 8;
+    ko[u] = (int64_t)tok * k_ts + head * D + hl * 8;
     if (slot[u] < slots) {
       vq[u].raw = ld_stream(q + qo[u]);
       vk[u].raw = ld_stream(k + ko[u]);
@@ -61,7 +67,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const bool ok = slot[u] < slots;
-    const int64_t token = ok ? (slot[u] / num_heads) % seq_len : 0;
+    const uint32_t tk = tokr[u];
+    const int64_t token = !ok ? 0 : (tk < (uint32_t)seq_len ? tk : tk % (uint32_t)seq_len);
     // cos/sin entries for this lane's 4 pairs: indices hl*4 .. hl*4+3.
     uint2 c2 = make_uint2(0, 0), s2 = make_uint2(0, 0);
     if (ROPE) {
@@ -184,6 +191,7 @@ extern "C" int jo_fused_qk_norm_rope_3d_paired(void* q, void* k, int64_t batch, 
   JO_REQUIRE(seq_len < (1LL << 31) && num_heads < (1LL << 31), JO_ERR_INVALID,
              "fused_qk_norm_rope_3d_paired: size too large");
   const int64_t slots = batch * seq_len * num_heads;
+  JO_REQUIRE(slots < (1LL << 31), JO_ERR_INVALID, "fused_qk_norm_rope_3d_paired: too many (token, head) slots");
   JO_REQUIRE(slots == 0 || (q && k && q_weight && k_weight && cos && sin), JO_ERR_INVALID,
              "fused_qk_norm_rope_3d_paired: null tensor pointer");
   JO_REQUIRE(aligned16(q) && aligned16(k) && aligned16(q_weight) && aligned16(k_weight) && aligned8(cos) &&
@@ -223,6 +231,7 @@ extern "C" int jo_qk_norm_rope_strided(void* q, void* k, int64_t batch, int64_t 
              JO_ERR_INVALID, "qk_norm_rope_strided: token strides must cover the heads and be multiples of 8");
   JO_REQUIRE((cos == nullptr) == (sin == nullptr), JO_ERR_INVALID, "qk_norm_rope_strided: give both cos and sin or neither");
   const int64_t slots = batch * seq_len * num_heads;
+  JO_REQUIRE(slots < (1LL << 31), JO_ERR_INVALID, "qk_norm_rope_strided: too many (token, head) slots");
   JO_REQUIRE(slots == 0 || (q && k && q_weight && k_weight), JO_ERR_INVALID, "qk_norm_rope_strided: null pointer");
   JO_REQUIRE(aligned16(q) && aligned16(k) && aligned16(q_weight) && aligned16(k_weight) &&
                  (!cos || (aligned8(cos) && aligned8(sin))),

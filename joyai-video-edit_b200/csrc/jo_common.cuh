@@ -149,6 +149,38 @@ __device__ __forceinline__ uint32_t absmax2(uint32_t acc, uint32_t w) {
 }
 __device__ __forceinline__ uint32_t absmax2_fold(uint32_t acc) { return max(acc & 0xffffu, acc >> 16); }
 
+// Running max of |elements| over packed 16-bit pairs in the floating-point
+// unit: one instruction per pair.  The result's sign bits are meaningless
+// (xorsign) and are masked by the fold; a NaN operand yields the canonical NaN
+// (0x7fff), whose masked pattern sorts above +inf, so the caller can flag it.
+template <typename T> __device__ __forceinline__ uint32_t absmax_h2(uint32_t acc, uint32_t w);
+template <> __device__ __forceinline__ uint32_t absmax_h2<__nv_bfloat16>(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w));
+  return r;
+}
+template <> __device__ __forceinline__ uint32_t absmax_h2<__half>(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w));
+  return r;
+}
+// Same without NaN propagation: a NaN operand yields the other operand, so the
+// result is the max of |x| over the non-NaN elements (as fmaxf reductions do).
+template <typename T> __device__ __forceinline__ uint32_t absmax_h2_nonan(uint32_t acc, uint32_t w);
+template <> __device__ __forceinline__ uint32_t absmax_h2_nonan<__nv_bfloat16>(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w));
+  return r;
+}
+template <> __device__ __forceinline__ uint32_t absmax_h2_nonan<__half>(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w));
+  return r;
+}
+__device__ __forceinline__ uint32_t absmax_h2_fold(uint32_t acc) {
+  return max(acc & 0x7fffu, (acc >> 16) & 0x7fffu);
+}
+
 // ---- paired fp32 arithmetic (sm_100: one instruction, two IEEE RN lanes) ----
 // Each lane is exactly the scalar fma.rn / mul.rn / add.rn of that lane.
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {

@@ -28,6 +28,7 @@
 #include "jo_common.cuh"
 
 #include <stdlib.h>
+#include <type_traits>
 
 namespace jo {
 namespace staged {
@@ -89,95 +90,92 @@ template <> __device__ __forceinline__ float2 unpack2_r<__nv_bfloat16>(uint32_t 
 
 // Team-wide reductions of R independent values (one per row).  Warp shuffles
 // first; teams spanning several warps meet in shared memory behind a named
-// barrier.  `red` slots must not be reused before the next barrier of the
-// following reduction (callers alternate slot sets by iteration parity).
+// barrier and every thread adds the warp partials in the same order.  `red`
+// slots must not be reused before the next barrier of the following reduction
+// (callers alternate slot sets by iteration parity).  `team` folds to a
+// constant in the fixed-geometry kernels, which unrolls the partial loop.
+template <int R, typename V, typename F>
+__device__ __forceinline__ void team_reduce(V (&v)[R], int team, int bar_id, V* red, F op) {
+  const int nw = team >> 5;
+  if (nw > 1) {
+    const int w = (threadIdx.x % team) >> 5;
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int r = 0; r < R; ++r) red[r * 16 + w] = v[r];
+    team_bar(bar_id, team);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      V t = red[r * 16];
+#pragma unroll
+      for (int i = 1; i < nw; ++i) t = op(t, red[r * 16 + i]);
+      v[r] = t;
+    }
+  }
+}
 template <int R>
 __device__ __forceinline__ void team_sum(float (&v)[R], int team, int bar_id, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
     for (int r = 0; r < R; ++r) v[r] += __shfl_xor_sync(0xffffffffu, v[r], o, 32);
-  const int nw = team >> 5;
-  if (nw > 1) {
-    const int w = (threadIdx.x % team) >> 5;
-    if ((threadIdx.x & 31) == 0)
-#pragma unroll
-      for (int r = 0; r < R; ++r) red[r * 16 + w] = v[r];
-    team_bar(bar_id, team);
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float t = red[r * 16];
-      for (int i = 1; i < nw; ++i) t += red[r * 16 + i];
-      v[r] = t;
-    }
-  }
-}
-template <int R>
-__device__ __forceinline__ void team_fmax(float (&v)[R], int team, int bar_id, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int r = 0; r < R; ++r) v[r] = fmaxf(v[r], __shfl_xor_sync(0xffffffffu, v[r], o, 32));
-  const int nw = team >> 5;
-  if (nw > 1) {
-    const int w = (threadIdx.x % team) >> 5;
-    if ((threadIdx.x & 31) == 0)
-#pragma unroll
-      for (int r = 0; r < R; ++r) red[r * 16 + w] = v[r];
-    team_bar(bar_id, team);
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float t = red[r * 16];
-      for (int i = 1; i < nw; ++i) t = fmaxf(t, red[r * 16 + i]);
-      v[r] = t;
-    }
-  }
+  team_reduce<R>(v, team, bar_id, red, [](float x, float y) { return x + y; });
 }
 template <int R>
 __device__ __forceinline__ void team_umax(uint32_t (&v)[R], int team, int bar_id, float* red) {
 #pragma unroll
   for (int r = 0; r < R; ++r) v[r] = __reduce_max_sync(0xffffffffu, v[r]);
-  const int nw = team >> 5;
-  if (nw > 1) {
-    uint32_t* rr = reinterpret_cast<uint32_t*>(red);
-    const int w = (threadIdx.x % team) >> 5;
-    if ((threadIdx.x & 31) == 0)
-#pragma unroll
-      for (int r = 0; r < R; ++r) rr[r * 16 + w] = v[r];
-    team_bar(bar_id, team);
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      uint32_t t = rr[r * 16];
-      for (int i = 1; i < nw; ++i) t = max(t, rr[r * 16 + i]);
-      v[r] = t;
-    }
-  }
+  team_reduce<R>(v, team, bar_id, reinterpret_cast<uint32_t*>(red),
+                 [](uint32_t x, uint32_t y) { return max(x, y); });
 }
 
-__device__ __forceinline__ float qval(float x, float inv) {
-  const float v = __fmul_rn(x, inv);
-  return fmaxf(fminf(v, kFp8Max), -kFp8Max);
+// Row statistics on the tensor cores.  One m16n8k16 MMA takes, per thread,
+// two words (four 16-bit elements) of ONE row as both the A fragment (rows
+// g = lane/4 of A; rows g + 8 are zero) and the B fragment (column g of B), so
+// the diagonal D[g][g] accumulates the sum of squares of the elements held by
+// the four threads of group g.  With B = ones instead, every D[g][n] holds the
+// plain sum of group g.  The products are exact in fp32 (16-bit inputs); only
+// the accumulation order differs from a scalar loop.
+template <typename T> struct MmaType;
+template <> struct MmaType<__nv_bfloat16> { static constexpr uint32_t kOnes = 0x3f803f80u; };
+template <> struct MmaType<__half> { static constexpr uint32_t kOnes = 0x3c003c00u; };
+template <typename T>
+__device__ __forceinline__ void mma_acc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a1), "r"(0u), "r"(b0), "r"(b1));
+  else
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a1), "r"(0u), "r"(b0), "r"(b1));
 }
+// This lane's share of the group sums: the diagonal element (sum of squares)
+// or column 0 (plain sum); zero on the other lanes.
+__device__ __forceinline__ float mma_diag(const float (&c)[4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
+  return (lane & 3) == (g >> 1) ? ((g & 1) ? c[1] : c[0]) : 0.f;
+}
+__device__ __forceinline__ float mma_col0(const float (&c)[4]) { return (threadIdx.x & 3) == 0 ? c[0] : 0.f; }
 
-// Codes of one 16-byte vector (8 elements in 4 words) -> 8 bytes.
-// FAST: x*inv is finite for every element (the row has no NaN/Inf and inv is
-// finite), so the e4m3 conversion's satfinite saturation equals the
-// reference's explicit clamp.  Otherwise the exact clamp form is used (it maps
-// NaN products to 448 as fminf/fmaxf do in the reference).
-template <typename T, bool FAST>
+// Codes of one 16-byte vector (8 elements in 4 words) -> 8 bytes:
+// e4m3(x * inv) with round-to-nearest-even and satfinite saturation.  For a
+// non-NaN product that equals the reference's explicit clamp to +-448 followed
+// by the conversion (an infinite product saturates to +-448 either way).
+template <typename T>
 __device__ __forceinline__ uint2 codes8(const uint4& v, float inv) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  uint32_t c[4];
+  float2 f[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float2 f = unpack2<T>(w[k]);
-    if (FAST) {
-      const float2 v = mul2(f, make_float2(inv, inv));
-      c[k] = pack_e4m3x2(v.x, v.y);
-    }
-    else c[k] = pack_e4m3x2(qval(f.x, inv), qval(f.y, inv));
-  }
-  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+  for (int k = 0; k < 4; ++k) f[k] = mul2(unpack2<T>(w[k]), make_float2(inv, inv));
+  return make_uint2(pack_e4m3x4(f[0].x, f[0].y, f[1].x, f[1].y), pack_e4m3x4(f[2].x, f[2].y, f[3].x, f[3].y));
+}
+// A NaN product converts to a NaN code (0x7f / 0xff), where the reference's
+// fminf/fmaxf clamp turns it into +448 (0x7e).  Rewrites those bytes.
+__device__ __forceinline__ uint32_t fix_nan_codes(uint32_t c) {
+  const uint32_t m = __vcmpeq4(c & 0x7f7f7f7fu, 0x7f7f7f7fu);  // 0xff in NaN bytes
+  return (c & ~m) | (0x7e7e7e7eu & m);
 }
 
 __device__ __forceinline__ void st_cs8(void* p, uint2 v) {
@@ -185,10 +183,11 @@ __device__ __forceinline__ void st_cs8(void* p, uint2 v) {
 }
 
 // Quantise R rows held in X (16-bit elements; bits[r] = team max of |x| as a
-// 16-bit pattern) and write codes + scales.
-template <typename T, int VPL, int R>
+// 16-bit pattern, NaN-flagging) and write codes + scales.  EXACT: the team
+// covers the row exactly (no index checks).
+template <typename T, int VPL, int R, bool EXACT>
 __device__ __forceinline__ void quant_rows(const Vec16<T> (&X)[R][VPL], const uint32_t (&bits)[R],
-                                           const int64_t (&row)[R], const bool (&ok)[R], uint8_t* q, float* sout,
+                                           const int64_t row0, const bool (&ok)[R], uint8_t* q, float* sout,
                                            int N, int team, int tl, int bar_id, float* red_slow) {
   const int nvec = N / 8;
   float amax[R];
@@ -199,61 +198,59 @@ __device__ __forceinline__ void quant_rows(const Vec16<T> (&X)[R][VPL], const ui
     any_slow |= !(bits[r] < Bits16<T>::kInf);
   }
   if (any_slow) {  // team-uniform: NaN or Inf in a row; reference amax ignores NaN (fmaxf)
+    uint32_t b2[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      float m = 0.f;
+      uint32_t acc = 0;  // never NaN: a NaN operand yields the other one
 #pragma unroll
-      for (int i = 0; i < VPL; ++i)
-        if (i * team + tl < nvec) {
-          const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack2<T>(w[k]);
-            m = fmaxf(m, fabsf(f.x));
-            m = fmaxf(m, fabsf(f.y));
-          }
-        }
-      amax[r] = m;
+      for (int i = 0; i < VPL; ++i) {
+        acc = absmax_h2_nonan<T>(acc, X[r][i].raw.x);
+        acc = absmax_h2_nonan<T>(acc, X[r][i].raw.y);
+        acc = absmax_h2_nonan<T>(acc, X[r][i].raw.z);
+        acc = absmax_h2_nonan<T>(acc, X[r][i].raw.w);
+      }
+      b2[r] = absmax_h2_fold(acc);
     }
-    team_fmax<R>(amax, team, bar_id, red_slow);
+    team_umax<R>(b2, team, bar_id, red_slow);
+#pragma unroll
+    for (int r = 0; r < R; ++r) amax[r] = from_bits16<T>(b2[r]);
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const float s = amax[r] / kFp8Max;
-    if (ok[r] && tl == 0) sout[row[r]] = s;
+    if (ok[r] && tl == 0) sout[row0 + r] = s;
     const float inv = s == 0.f ? 0.f : __frcp_rn(s);
     const bool fast = (bits[r] < Bits16<T>::kInf) && inv < __int_as_float(0x7f800000);
     if (!ok[r]) continue;
-    uint8_t* qr = q + row[r] * (int64_t)N;
-    if (fast) {
+    uint8_t* qr = q + (row0 + r) * (int64_t)N + tl * 8;
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int idx = i * team + tl;
-        if (idx < nvec) st_cs8(qr + (int64_t)idx * 8, codes8<T, true>(X[r][i].raw, inv));
+    for (int i = 0; i < VPL; ++i)
+      if (EXACT || i * team + tl < nvec) {
+        uint2 c = codes8<T>(X[r][i].raw, inv);
+        if (!fast) c = make_uint2(fix_nan_codes(c.x), fix_nan_codes(c.y));
+        st_cs8(qr + i * team * 8, c);
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int idx = i * team + tl;
-        if (idx < nvec) st_cs8(qr + (int64_t)idx * 8, codes8<T, false>(X[r][i].raw, inv));
-      }
-    }
   }
 }
 
 constexpr int staged_max_threads(int vpl, int r) { return vpl * r >= 10 ? 256 : vpl * r == 8 ? 640 : 512; }
 
-template <typename T, int OP, int NORM, int VPL, int S, int R>
+// NW > 0: the team is NW warps and covers a row exactly (N = VPL * NW * 256,
+// checked by the host), so every index check folds away and every address
+// offset within a row is an immediate.  NW == 0: run-time team size.
+template <typename T, int OP, int NORM, int VPL, int S, int R, int NW>
 __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
-    staged_rows(const Args a, const int team, const int teams) {
+    staged_rows(const Args a, const int team_rt, const int teams) {
   constexpr bool HAS_NORM = (OP != OP_QUANT);
+  constexpr bool EXACT = NW > 0;
   extern __shared__ __align__(16) unsigned char smem_raw[];
 
-  const int N = a.N;
-  const int nvec = N / 8;
+  const int team = EXACT ? NW * 32 : team_rt;
+  const int nvec = EXACT ? VPL * NW * 32 : a.N / 8;
+  const int N = nvec * 8;
   const int tid = threadIdx.x;
-  const int tm = tid / team;   // team in CTA
-  const int tl = tid % team;   // thread in team
+  const int tm = tid / team;       // team in CTA
+  const int tl = tid - tm * team;  // thread in team
   const int bar_id = 1 + tm;
 
   // ---- fp32 tables -------------------------------------------------------
@@ -294,8 +291,9 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
   const int64_t ngroups = (M + R - 1) / R;
   const int64_t gteam = (int64_t)blockIdx.x * teams + tm;
   const int64_t tstride = (int64_t)gridDim.x * teams;
-  const char* xb = static_cast<const char*>(a.x);
+  const char* xb = static_cast<const char*>(a.x) + tl * 16;
   const int64_t rowb = (int64_t)N * sizeof(T);
+  uint4* ring_t = ring + tl;
 
   auto issue = [&](int64_t grp, int stage) {
     if (grp < ngroups) {
@@ -304,12 +302,10 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
         const int64_t row = grp * R + r;
         if (row < M) {
           const char* src = xb + row * rowb;
-          uint4* dst = ring + (size_t)(stage * R + r) * nvec;
+          uint4* dst = ring_t + (size_t)(stage * R + r) * nvec;
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) {
-            const int idx = i * team + tl;
-            if (idx < nvec) cp_async16(dst + idx, src + (int64_t)idx * 16);
-          }
+          for (int i = 0; i < VPL; ++i)
+            if (EXACT || i * team + tl < nvec) cp_async16(dst + i * team, src + i * team * 16);
         }
       }
     }
@@ -325,18 +321,15 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
     issue(grp + (int64_t)(S - 1) * tstride, (stage + S - 1) % S);
     cp_wait<S - 1>();
     Vec16<T> X[R][VPL];
-    int64_t row[R];
+    const int64_t row0 = grp * R;
     bool ok[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      row[r] = grp * R + r;
-      ok[r] = row[r] < M;
-      const uint4* src = ring + (size_t)(stage * R + r) * nvec;
+      ok[r] = row0 + r < M;
+      const uint4* src = ring_t + (size_t)(stage * R + r) * nvec;
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int idx = i * team + tl;
-        X[r][i].raw = (ok[r] && idx < nvec) ? lds16(src + idx) : make_uint4(0, 0, 0, 0);
-      }
+      for (int i = 0; i < VPL; ++i)
+        X[r][i].raw = (ok[r] && (EXACT || i * team + tl < nvec)) ? lds16(src + i * team) : make_uint4(0, 0, 0, 0);
     }
     stage = (stage + 1 == S) ? 0 : stage + 1;
 
@@ -347,32 +340,30 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
         uint32_t acc = 0;
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
-          acc = absmax2(acc, X[r][i].raw.x);
-          acc = absmax2(acc, X[r][i].raw.y);
-          acc = absmax2(acc, X[r][i].raw.z);
-          acc = absmax2(acc, X[r][i].raw.w);
+          acc = absmax_h2<T>(acc, X[r][i].raw.x);
+          acc = absmax_h2<T>(acc, X[r][i].raw.y);
+          acc = absmax_h2<T>(acc, X[r][i].raw.z);
+          acc = absmax_h2<T>(acc, X[r][i].raw.w);
         }
-        bits[r] = absmax2_fold(acc);
+        bits[r] = absmax_h2_fold(acc);
       }
       team_umax<R>(bits, team, bar_id, red[parity][0]);
-      quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[parity][1]);
+      quant_rows<T, VPL, R, EXACT>(X, bits, row0, ok, a.q, a.s, N, team, tl, bar_id, red[parity][1]);
     } else {
-      // Row statistics: each thread accumulates its elements in two fp32
-      // chains (even / odd element of every pair, one paired instruction per
-      // pair), the chains are added, then the team reduces.
+      // Row statistics on the tensor cores (two accumulator chains per row),
+      // then the team reduction.  Zero-filled tail vectors add nothing.
       float mean[R], rr[R];
       if constexpr (NORM == JO_NORM_LAYER) {
         float sum[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          float2 s2 = make_float2(0.f, 0.f);
+          float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int i = 0; i < VPL; ++i) {
-            const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) s2 = add2(s2, unpack2_r<T>(w[k]));
+            mma_acc<T>(ca, X[r][i].raw.x, X[r][i].raw.y, MmaType<T>::kOnes, MmaType<T>::kOnes);
+            mma_acc<T>(cb, X[r][i].raw.z, X[r][i].raw.w, MmaType<T>::kOnes, MmaType<T>::kOnes);
           }
-          sum[r] = s2.x + s2.y;
+          sum[r] = mma_col0(ca) + mma_col0(cb);
         }
         team_sum<R>(sum, team, bar_id, red[parity][0]);
         float ss[R];
@@ -383,7 +374,7 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
           float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < VPL; ++i)
-            if (i * team + tl < nvec) {
+            if (EXACT || i * team + tl < nvec) {
               const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
@@ -401,17 +392,13 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           mean[r] = 0.f;
-          float2 q2 = make_float2(0.f, 0.f);
+          float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int i = 0; i < VPL; ++i) {
-            const uint32_t w[4] = {X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.z, X[r][i].raw.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack2_r<T>(w[k]);
-              q2 = fma2(f, f, q2);
-            }
+            mma_acc<T>(ca, X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.x, X[r][i].raw.y);
+            mma_acc<T>(cb, X[r][i].raw.z, X[r][i].raw.w, X[r][i].raw.z, X[r][i].raw.w);
           }
-          ss[r] = q2.x + q2.y;
+          ss[r] = mma_diag(ca) + mma_diag(cb);
         }
         team_sum<R>(ss, team, bar_id, red[parity][0]);
 #pragma unroll
@@ -425,11 +412,10 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
       for (int r = 0; r < R; ++r) acc[r] = 0;
 #pragma unroll
       for (int i = 0; i < VPL; ++i) {
-        const int idx = i * team + tl;
-        if (idx >= nvec) continue;
+        if (!(EXACT || i * team + tl < nvec)) continue;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int c = h * (N >> 1) + 4 * idx;
+          const int c = h * (N >> 1) + 4 * (i * team + tl);
           const float4 g = lds16f(tg + c);
           const float4 sc = lds16f(tsc + c);
           const float4 sh = lds16f(tsh + c);
@@ -456,8 +442,8 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
             wr[2 * h] = pack2<T>(f0.x, f0.y);      // RNE to T, as the reference's T(float) store
             wr[2 * h + 1] = pack2<T>(f1.x, f1.y);
             if constexpr (OP == OP_NORM_MOD_QUANT) {
-              acc[r] = absmax2(acc[r], wr[2 * h]);
-              acc[r] = absmax2(acc[r], wr[2 * h + 1]);
+              acc[r] = absmax_h2<T>(acc[r], wr[2 * h]);
+              acc[r] = absmax_h2<T>(acc[r], wr[2 * h + 1]);
             }
           }
         }
@@ -466,31 +452,30 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           if (!ok[r]) continue;
-          char* yr = static_cast<char*>(a.y) + row[r] * rowb;
+          char* yr = static_cast<char*>(a.y) + (row0 + r) * rowb + tl * 16;
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) {
-            const int idx = i * team + tl;
-            if (idx < nvec) st_stream(yr + (int64_t)idx * 16, X[r][i].raw);
-          }
+          for (int i = 0; i < VPL; ++i)
+            if (EXACT || i * team + tl < nvec) st_stream(yr + i * team * 16, X[r][i].raw);
         }
       } else {
         uint32_t bits[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) bits[r] = absmax2_fold(acc[r]);
+        for (int r = 0; r < R; ++r) bits[r] = absmax_h2_fold(acc[r]);
         team_umax<R>(bits, team, bar_id, red[parity][2]);
-        quant_rows<T, VPL, R>(X, bits, row, ok, a.q, a.s, N, team, tl, bar_id, red[parity][3]);
+        quant_rows<T, VPL, R, EXACT>(X, bits, row0, ok, a.q, a.s, N, team, tl, bar_id, red[parity][3]);
       }
     }
   }
   cp_wait<0>();
 }
 
-template <typename T, int OP, int NORM, int VPL, int S, int R>
+template <typename T, int OP, int NORM, int VPL, int S, int R, int NW>
 int launch(const Args& a, int team, cudaStream_t st) {
   const int nvec = a.N / 8;
+  if (NW > 0 && (team != NW * 32 || nvec != VPL * NW * 32)) return JO_ERR_INVALID;
   const size_t tab = (OP != OP_QUANT) ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
   const size_t per_team = (size_t)S * R * nvec * 16 + (size_t)2 * 4 * R * 16 * sizeof(float);
-  // Up to 512 threads and ~200 KB of shared memory per CTA, one CTA per SM.
+  // Up to 640 threads and ~224 KB of shared memory per CTA, one CTA per SM.
   int teams = staged_max_threads(VPL, R) / team;
   if (teams > kMaxTeams) teams = kMaxTeams;
   while (teams > 1 && tab + teams * per_team > 224 * 1024) --teams;
@@ -498,13 +483,13 @@ int launch(const Args& a, int team, cudaStream_t st) {
   if (smem > 224 * 1024) return JO_ERR_INVALID;
   static size_t attr = 0;
   if (attr < smem) {
-    cudaFuncSetAttribute(staged_rows<T, OP, NORM, VPL, S, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(staged_rows<T, OP, NORM, VPL, S, R, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
     attr = smem;
   }
   const int64_t need = ((a.M + R - 1) / R + teams - 1) / teams;
   const int64_t grid = need < sm_count() ? need : sm_count();
-  staged_rows<T, OP, NORM, VPL, S, R><<<(unsigned)grid, team * teams, smem, st>>>(a, team, teams);
+  staged_rows<T, OP, NORM, VPL, S, R, NW><<<(unsigned)grid, team * teams, smem, st>>>(a, team, teams);
   return JO_OK;
 }
 
@@ -535,22 +520,34 @@ static StagedGeom pick_geom(int nvec) {
   return StagedGeom{4, 2, 2};
 }
 
+// JO_STAGED_FIXED=0 disables the fixed-geometry instantiations (comparison).
+static bool fixed_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("JO_STAGED_FIXED");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 template <typename T, int OP, int NORM>
 static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream_t st) {
   using namespace staged;
   const int team = ((nvec + g.vpl - 1) / g.vpl + 31) / 32 * 32;
   if (team > 512) return JO_ERR_INVALID;
+  // Fixed geometries for the model's widths: N = 5120 (hidden) and 3072.
+  if (g.vpl == 4 && g.r == 2 && g.s == 2 && team * 4 == nvec && fixed_enabled()) {
+    if (team == 160) return launch<T, OP, NORM, 4, 2, 2, 5>(a, team, st);
+    if (team == 96) return launch<T, OP, NORM, 4, 2, 2, 3>(a, team, st);
+  }
 #define JO_G(V, R, S) \
-  if (g.vpl == V && g.r == R && g.s == S) return launch<T, OP, NORM, V, S, R>(a, team, st);
+  if (g.vpl == V && g.r == R && g.s == S) return launch<T, OP, NORM, V, S, R, 0>(a, team, st);
   JO_G(4, 2, 2)
   JO_G(4, 1, 3)
   JO_G(10, 1, 2)
-  JO_G(10, 1, 3)
   JO_G(20, 1, 2)
-  JO_G(20, 1, 3)
-  JO_G(8, 2, 2)
 #undef JO_G
-  return launch<T, OP, NORM, 4, 2, 2>(a, ((nvec + 3) / 4 + 31) / 32 * 32, st);
+  return launch<T, OP, NORM, 4, 2, 2, 0>(a, ((nvec + 3) / 4 + 31) / 32 * 32, st);
 }
 
 // Entry used by row_ops.cu.  Returns JO_ERR_INVALID (no launch) when the shape

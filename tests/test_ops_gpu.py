@@ -124,7 +124,9 @@ def test_fused_norm_scale_shift_broadcast_view(jo, cuda):
                                   "rms", 1e-6)
     y2 = jo.fused_norm_scale_shift(to_torch(x, "bf16", cuda), None, None, sct.expand(M, N).contiguous(),
                                    sht.expand(M, N).contiguous(), "rms", 1e-6)
-    assert torch.equal(y, y2)
+    # The view takes the staged kernel (tensor-core row statistics), the dense
+    # table the register kernel: same formula, different summation order.
+    assert_close_ulp(to_np(y), to_np(y2), max_ulp=1)
     assert_close_ulp(to_np(y), O.fused_norm_scale_shift(x, None, None, sc, sh, 1, 1e-6))
 
 

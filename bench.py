@@ -287,7 +287,7 @@ def run_ours(args):
             "gpu_launches": K,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": args.traffic,
-                         "peak_source": pk["source"], "kernel": "staged_rows<bf16,NORM_MOD_QUANT,RMS,4,2,2>",
+                         "peak_source": pk["source"], "kernel": "staged_rows<bf16,NORM_MOD_QUANT,RMS,vpl5,S2,R2,4 warps>",
                          "avg_launch_us": round(avg_launch_us, 3)},
             "clocks": clocks,
         }

@@ -217,7 +217,7 @@ __device__ __forceinline__ void quant_rows(const Vec16<T> (&X)[R][VPL], const ui
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const float s = amax[r] / kFp8Max;
+    const float s = div448_h(amax[r]);  // == amax / 448 (amax is a 16-bit value)
     if (ok[r] && tl == 0) sout[row0 + r] = s;
     const float inv = s == 0.f ? 0.f : __frcp_rn(s);
     const bool fast = (bits[r] < Bits16<T>::kInf) && inv < __int_as_float(0x7f800000);
@@ -234,12 +234,27 @@ __device__ __forceinline__ void quant_rows(const Vec16<T> (&X)[R][VPL], const ui
 }
 
 constexpr int staged_max_threads(int vpl, int r) { return vpl * r >= 10 ? 256 : vpl * r == 8 ? 640 : 512; }
+// Fixed geometries: N = VPL * NW * 256 is known at compile time, so the
+// number of teams per CTA is too: as many as the shared memory holds (fp32
+// tables + S * R rows of ring + reduction scratch per team), at most 1024
+// threads and kMaxTeams teams.
+constexpr int fixed_teams(int op, int norm, int vpl, int s, int r, int nw) {
+  const int n = vpl * nw * 256;
+  const int tab = op == OP_QUANT ? 0 : (norm == JO_NORM_LAYER ? 4 : 3) * n * 4;
+  const int per_team = s * r * n * 2 + 2 * 4 * r * 16 * 4;
+  int t = (224 * 1024 - tab) / per_team;
+  if (t * nw * 32 > 1024) t = 1024 / (nw * 32);
+  return t > kMaxTeams ? kMaxTeams : t;
+}
+constexpr int staged_threads(int op, int norm, int vpl, int s, int r, int nw) {
+  return nw == 0 ? staged_max_threads(vpl, r) : fixed_teams(op, norm, vpl, s, r, nw) * nw * 32;
+}
 
 // NW > 0: the team is NW warps and covers a row exactly (N = VPL * NW * 256,
 // checked by the host), so every index check folds away and every address
 // offset within a row is an immediate.  NW == 0: run-time team size.
 template <typename T, int OP, int NORM, int VPL, int S, int R, int NW>
-__global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
+__global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
     staged_rows(const Args a, const int team_rt, const int teams) {
   constexpr bool HAS_NORM = (OP != OP_QUANT);
   constexpr bool EXACT = NW > 0;
@@ -252,6 +267,9 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
   const int tm = tid / team;       // team in CTA
   const int tl = tid - tm * team;  // thread in team
   const int bar_id = 1 + tm;
+  // 1/N once: the row statistics scale by it (within 1 ulp of a division; the
+  // tensor-core sums already differ from a scalar loop in summation order).
+  const float inv_n = 1.f / (float)N;
 
   // ---- fp32 tables -------------------------------------------------------
   constexpr int NTAB = HAS_NORM ? (NORM == JO_NORM_LAYER ? 4 : 3) : 0;
@@ -329,7 +347,9 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
       const uint4* src = ring_t + (size_t)(stage * R + r) * nvec;
 #pragma unroll
       for (int i = 0; i < VPL; ++i)
-        X[r][i].raw = (ok[r] && (EXACT || i * team + tl < nvec)) ? lds16(src + i * team) : make_uint4(0, 0, 0, 0);
+        // EXACT: rows past M read stale ring data; nothing of them is stored.
+        X[r][i].raw = EXACT ? lds16(src + i * team)
+                            : (ok[r] && i * team + tl < nvec) ? lds16(src + i * team) : make_uint4(0, 0, 0, 0);
     }
     stage = (stage + 1 == S) ? 0 : stage + 1;
 
@@ -369,7 +389,7 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
         float ss[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          mean[r] = sum[r] / (float)N;
+          mean[r] = sum[r] * inv_n;
           const float2 nm = make_float2(-mean[r], -mean[r]);
           float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -386,7 +406,7 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
         }
         team_sum<R>(ss, team, bar_id, red[parity][1]);
 #pragma unroll
-        for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
+        for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] * inv_n + a.eps);
       } else {
         float ss[R];
 #pragma unroll
@@ -402,7 +422,7 @@ __global__ void __launch_bounds__(staged_max_threads(VPL, R), 1)
         }
         team_sum<R>(ss, team, bar_id, red[parity][0]);
 #pragma unroll
-        for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] / (float)N + a.eps);
+        for (int r = 0; r < R; ++r) rr[r] = rsqrtf(ss[r] * inv_n + a.eps);
       }
       // y = ((x - mean) * r * g + b) * (1 + sc) + sh  (layer)
       // y = (x * r * g) * (1 + sc) + sh                (rms)
@@ -476,8 +496,9 @@ int launch(const Args& a, int team, cudaStream_t st) {
   const size_t tab = (OP != OP_QUANT) ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
   const size_t per_team = (size_t)S * R * nvec * 16 + (size_t)2 * 4 * R * 16 * sizeof(float);
   // Up to 640 threads and ~224 KB of shared memory per CTA, one CTA per SM.
-  int teams = staged_max_threads(VPL, R) / team;
+  int teams = NW > 0 ? fixed_teams(OP, NORM, VPL, S, R, NW) : staged_max_threads(VPL, R) / team;
   if (teams > kMaxTeams) teams = kMaxTeams;
+  if (teams < 1) return JO_ERR_INVALID;  // team wider than the CTA budget: caller falls back
   while (teams > 1 && tab + teams * per_team > 224 * 1024) --teams;
   const size_t smem = tab + teams * per_team;
   if (smem > 224 * 1024) return JO_ERR_INVALID;
@@ -516,7 +537,9 @@ static StagedGeom pick_geom(int nvec) {
     }
   }
   if (ov == 1) return g_ov;
-  (void)nvec;
+  // N = 5120: 4-warp teams of 5 vectors per thread, two rows per iteration
+  // (fixed-geometry instantiation; measured best of the fixed set).
+  if (nvec == 640) return StagedGeom{5, 2, 2};
   return StagedGeom{4, 2, 2};
 }
 
@@ -530,6 +553,7 @@ static bool fixed_enabled() {
   return v == 1;
 }
 
+#define N_FIXED_OK(g, nvec) ((nvec) == 640)
 template <typename T, int OP, int NORM>
 static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream_t st) {
   using namespace staged;
@@ -539,6 +563,15 @@ static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream
   if (g.vpl == 4 && g.r == 2 && g.s == 2 && team * 4 == nvec && fixed_enabled()) {
     if (team == 160) return launch<T, OP, NORM, 4, 2, 2, 5>(a, team, st);
     if (team == 96) return launch<T, OP, NORM, 4, 2, 2, 3>(a, team, st);
+  }
+  if (fixed_enabled() && N_FIXED_OK(g, nvec)) {
+#define JO_F(V, R, S, W) \
+  if (g.vpl == V && g.r == R && g.s == S && nvec == V * W * 32) return launch<T, OP, NORM, V, S, R, W>(a, team, st);
+    JO_F(4, 1, 2, 5)
+    JO_F(5, 1, 2, 4)
+    JO_F(5, 2, 2, 4)
+    JO_F(10, 1, 2, 2)
+#undef JO_F
   }
 #define JO_G(V, R, S) \
   if (g.vpl == V && g.r == R && g.s == S) return launch<T, OP, NORM, V, S, R, 0>(a, team, st);

@@ -231,3 +231,32 @@ def test_torch_eager_cpu_path_agrees_with_oracle():
     oq, os_ = O.per_token_quant_fp8(y)
     assert np.allclose(s.view(-1).numpy(), os_, rtol=1e-5)
     assert (q.view(torch.uint8).numpy() != oq).mean() < 2e-3
+
+
+def _rn32(fr):
+    """Round an exact rational to float32 (nearest, ties to even)."""
+    from fractions import Fraction
+    f = np.float32(float(fr))
+    best, bd = f, abs(Fraction(float(f)) - fr)
+    for c in (np.nextafter(f, np.float32(np.inf)), np.nextafter(f, np.float32(-np.inf))):
+        d = abs(Fraction(float(c)) - fr)
+        if d < bd or (d == bd and (c.view(np.uint32) & 1) == 0):
+            best, bd = c, d
+    return best
+
+
+def test_div448_fma_sequence_exact_for_16bit_inputs():
+    """The staged kernel forms the per-token scale amax / 448 as
+    q = a * RN(1/448); r = fma(-q, 448, a); q + r * RN(1/448) (each step one
+    IEEE rounding).  For every finite positive bf16 / fp16 amax that equals the
+    correctly rounded quotient the reference computes."""
+    from fractions import Fraction as F
+    c = _rn32(F(1, 448))
+    assert c == np.float32(1) / np.float32(448)
+    for vals in ((np.arange(1, 0x7f80, dtype=np.uint32) << 16).view(np.float32),
+                 np.arange(1, 0x7c00, dtype=np.uint16).view(np.float16).astype(np.float32)):
+        for a in vals:
+            A = F(float(a))
+            q = _rn32(A * F(float(c)))
+            r = _rn32(A - F(float(q)) * 448)
+            assert _rn32(F(float(r)) * F(float(c)) + F(float(q))) == _rn32(A / 448), a

@@ -128,36 +128,53 @@ __device__ __forceinline__ void team_umax(uint32_t (&v)[R], int team, int bar_id
                  [](uint32_t x, uint32_t y) { return max(x, y); });
 }
 
-// Row statistics on the tensor cores.  One m16n8k16 MMA takes, per thread,
-// two words (four 16-bit elements) of ONE row as both the A fragment (rows
-// g = lane/4 of A; rows g + 8 are zero) and the B fragment (column g of B), so
-// the diagonal D[g][g] accumulates the sum of squares of the elements held by
-// the four threads of group g.  With B = ones instead, every D[g][n] holds the
-// plain sum of group g.  The products are exact in fp32 (16-bit inputs); only
-// the accumulation order differs from a scalar loop.
+// Row statistics on the tensor cores, m16n8k8 with fp32 accumulation.  Per
+// thread the A fragment is one register pair (row g = lane/4 and row g + 8 of
+// A, two 16-bit elements each) and B one register (column g).  With A = {u, v}
+// (two words of ONE row, as loaded: no register moves) and B = u, the
+// diagonal D[g][g] gains the squares of u over the four threads of group g
+// (rows g + 8 gain cross products u*v, unused); with B = v, D[g+8][g] gains
+// the squares of v (rows g gain cross products).  The two forms therefore
+// accumulate in separate registers.  With B = ones, every D[g][n] gains the
+// plain sum of u of group g and D[g+8][n] that of v.  The products are exact
+// in fp32 (16-bit inputs); only the accumulation order differs from a scalar
+// loop.
 template <typename T> struct MmaType;
 template <> struct MmaType<__nv_bfloat16> { static constexpr uint32_t kOnes = 0x3f803f80u; };
 template <> struct MmaType<__half> { static constexpr uint32_t kOnes = 0x3c003c00u; };
 template <typename T>
-__device__ __forceinline__ void mma_acc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_k8(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value)
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a1), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(b));
   else
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a1), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(b));
 }
-// This lane's share of the group sums: the diagonal element (sum of squares)
-// or column 0 (plain sum); zero on the other lanes.
-__device__ __forceinline__ float mma_diag(const float (&c)[4]) {
+// Sum of squares of one 16-byte vector: words x, z into the top diagonal of
+// cu, words y, w into the bottom diagonal of cv.
+template <typename T>
+__device__ __forceinline__ void mma_sumsq(float (&cu)[4], float (&cv)[4], const uint4& v) {
+  mma_k8<T>(cu, v.x, v.y, v.x);
+  mma_k8<T>(cv, v.x, v.y, v.y);
+  mma_k8<T>(cu, v.z, v.w, v.z);
+  mma_k8<T>(cv, v.z, v.w, v.w);
+}
+// Plain sum of one 16-byte vector into c (column 0 of rows g and g + 8).
+template <typename T>
+__device__ __forceinline__ void mma_sum(float (&c)[4], const uint4& v) {
+  mma_k8<T>(c, v.x, v.y, MmaType<T>::kOnes);
+  mma_k8<T>(c, v.z, v.w, MmaType<T>::kOnes);
+}
+// This lane's share of the squares: D[g][g] of cu plus D[g+8][g] of cv; of
+// the plain sums: D[g][0] + D[g+8][0]; zero on the other lanes.
+__device__ __forceinline__ float mma_diag(const float (&cu)[4], const float (&cv)[4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2;
-  return (lane & 3) == (g >> 1) ? ((g & 1) ? c[1] : c[0]) : 0.f;
+  return (lane & 3) == (g >> 1) ? ((g & 1) ? cu[1] + cv[3] : cu[0] + cv[2]) : 0.f;
 }
-__device__ __forceinline__ float mma_col0(const float (&c)[4]) { return (threadIdx.x & 3) == 0 ? c[0] : 0.f; }
+__device__ __forceinline__ float mma_col0(const float (&c)[4]) { return (threadIdx.x & 3) == 0 ? c[0] + c[2] : 0.f; }
 
 // Codes of one 16-byte vector (8 elements in 4 words) -> 8 bytes:
 // e4m3(x * inv) with round-to-nearest-even and satfinite saturation.  For a
@@ -379,10 +396,7 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
         for (int r = 0; r < R; ++r) {
           float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) {
-            mma_acc<T>(ca, X[r][i].raw.x, X[r][i].raw.y, MmaType<T>::kOnes, MmaType<T>::kOnes);
-            mma_acc<T>(cb, X[r][i].raw.z, X[r][i].raw.w, MmaType<T>::kOnes, MmaType<T>::kOnes);
-          }
+          for (int i = 0; i < VPL; ++i) mma_sum<T>((i & 1) ? cb : ca, X[r][i].raw);
           sum[r] = mma_col0(ca) + mma_col0(cb);
         }
         team_sum<R>(sum, team, bar_id, red[parity][0]);
@@ -414,11 +428,8 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
           mean[r] = 0.f;
           float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) {
-            mma_acc<T>(ca, X[r][i].raw.x, X[r][i].raw.y, X[r][i].raw.x, X[r][i].raw.y);
-            mma_acc<T>(cb, X[r][i].raw.z, X[r][i].raw.w, X[r][i].raw.z, X[r][i].raw.w);
-          }
-          ss[r] = mma_diag(ca) + mma_diag(cb);
+          for (int i = 0; i < VPL; ++i) mma_sumsq<T>(ca, cb, X[r][i].raw);
+          ss[r] = mma_diag(ca, cb);
         }
         team_sum<R>(ss, team, bar_id, red[parity][0]);
 #pragma unroll

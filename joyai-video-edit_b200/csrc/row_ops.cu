@@ -25,11 +25,13 @@
 
 namespace jo {
 int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, const void* gamma, const void* beta,
-                       const void* scale, const void* shift, uint8_t* q, float* s, int64_t M, int N, float eps,
-                       cudaStream_t st);
+                       const void* scale, const void* shift, int64_t mod_stride, int64_t mod_group, uint8_t* q,
+                       float* s, int64_t M, int N, float eps, cudaStream_t st);
 namespace {
 
 enum RowOp : int { OP_NORM_MOD = 0, OP_RMSNORM = 1, OP_QUANT = 2, OP_NORM_MOD_QUANT = 3 };
+constexpr int STAGED_NORM_MODROW = 4;        // staged kernel: per-row scale / shift rows
+constexpr int STAGED_NORM_MODROW_QUANT = 5;  // the same, quantised
 
 struct RowArgs {
   const void* x;
@@ -558,8 +560,14 @@ int jo_fused_norm_scale_shift(void* y, const void* x, const void* gamma, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool broadcast = (mod_stride == 0 || mod_group >= M) && x_stride == N;
   if (vec_ok && broadcast &&
-      staged_rows_launch(OP_NORM_MOD, norm_type, dtype, x, y, gamma, beta, scale, shift, nullptr, nullptr, M,
+      staged_rows_launch(OP_NORM_MOD, norm_type, dtype, x, y, gamma, beta, scale, shift, 0, 1, nullptr, nullptr, M,
                          (int)N, eps, s) == JO_OK)
+    return check_launch(what);
+  // Per-row (or per-group) modulation rows: the staged kernel streams x,
+  // scale and shift rows together through its cp.async ring.
+  if (vec_ok && x_stride == N &&
+      staged_rows_launch(STAGED_NORM_MODROW, norm_type, dtype, x, y, gamma, beta, scale, shift, mod_stride,
+                         mod_group, nullptr, nullptr, M, (int)N, eps, s) == JO_OK)
     return check_launch(what);
   return norm_type == JO_NORM_LAYER ? dispatch_dtype<OP_NORM_MOD, JO_NORM_LAYER>(dtype, a, vec_ok, s, what)
                                     : dispatch_dtype<OP_NORM_MOD, JO_NORM_RMS>(dtype, a, vec_ok, s, what);
@@ -603,7 +611,7 @@ int jo_per_token_quant_fp8(const void* input, int in_dtype, void* out_q, float* 
             static_cast<uint8_t*>(out_q), out_s, M, (int)K, 0.f};
   const bool vec_ok = aligned16(input) && aligned8(out_q) && (K % 8) == 0;
   if (vec_ok && staged_rows_launch(OP_QUANT, JO_NORM_RMS, in_dtype, input, nullptr, nullptr, nullptr, nullptr,
-                                   nullptr, static_cast<uint8_t*>(out_q), out_s, M, (int)K, 0.f, s) == JO_OK)
+                                   nullptr, 0, 1, static_cast<uint8_t*>(out_q), out_s, M, (int)K, 0.f, s) == JO_OK)
     return check_launch(what);
   return dispatch_dtype<OP_QUANT, JO_NORM_RMS>(in_dtype, a, vec_ok, s, what);
 }
@@ -636,8 +644,12 @@ int jo_norm_modulate_quant_fp8(const void* x, const void* gamma, const void* bet
                       ((mod_stride * 2) % 16 == 0);
   const bool broadcast = mod_stride == 0 || mod_group >= M;
   if (vec_ok && broadcast &&
-      staged_rows_launch(OP_NORM_MOD_QUANT, norm_type, dtype, x, nullptr, gamma, beta, scale, shift,
+      staged_rows_launch(OP_NORM_MOD_QUANT, norm_type, dtype, x, nullptr, gamma, beta, scale, shift, 0, 1,
                          static_cast<uint8_t*>(out_q), out_s, M, (int)N, eps, s) == JO_OK)
+    return check_launch(what);
+  if (vec_ok && !broadcast &&
+      staged_rows_launch(STAGED_NORM_MODROW_QUANT, norm_type, dtype, x, nullptr, gamma, beta, scale, shift,
+                         mod_stride, mod_group, static_cast<uint8_t*>(out_q), out_s, M, (int)N, eps, s) == JO_OK)
     return check_launch(what);
   return norm_type == JO_NORM_LAYER ? dispatch_dtype<OP_NORM_MOD_QUANT, JO_NORM_LAYER>(dtype, a, vec_ok, s, what)
                                     : dispatch_dtype<OP_NORM_MOD_QUANT, JO_NORM_RMS>(dtype, a, vec_ok, s, what);

@@ -33,7 +33,12 @@
 namespace jo {
 namespace staged {
 
-enum : int { OP_NORM_MOD = 0, OP_QUANT = 2, OP_NORM_MOD_QUANT = 3 };
+// OP_NORM_MODROW: norm -> modulate with per-row [M, N] scale / shift rows,
+// staged through the ring beside x (three rows per ring slot).
+// OP_NORM_MODROW_QUANT: the same followed by per-token e4m3 quantisation.
+// Modulation row of token `row`: row / mod_group, mod_stride elements apart.
+enum : int { OP_NORM_MOD = 0, OP_QUANT = 2, OP_NORM_MOD_QUANT = 3, OP_NORM_MODROW = 4, OP_NORM_MODROW_QUANT = 5 };
+constexpr bool is_modrow(int op) { return op == OP_NORM_MODROW || op == OP_NORM_MODROW_QUANT; }
 constexpr int kMaxTeams = 15;  // teams per CTA (named barriers 1..15)
 
 struct Args {
@@ -45,6 +50,8 @@ struct Args {
   const void* shift;  // [N] broadcast
   uint8_t* q;
   float* s;
+  int64_t mod_stride;  // per-row modulation (OP_NORM_MODROW*): elements between rows
+  int64_t mod_group;   // tokens sharing one modulation row
   int64_t M;
   int N;
   float eps;
@@ -257,8 +264,8 @@ constexpr int staged_max_threads(int vpl, int r) { return vpl * r >= 10 ? 256 : 
 // threads and kMaxTeams teams.
 constexpr int fixed_teams(int op, int norm, int vpl, int s, int r, int nw) {
   const int n = vpl * nw * 256;
-  const int tab = op == OP_QUANT ? 0 : (norm == JO_NORM_LAYER ? 4 : 3) * n * 4;
-  const int per_team = s * r * n * 2 + 2 * 4 * r * 16 * 4;
+  const int tab = (op == OP_QUANT || is_modrow(op)) ? 0 : (norm == JO_NORM_LAYER ? 4 : 3) * n * 4;
+  const int per_team = s * r * n * 2 * (is_modrow(op) ? 3 : 1) + 2 * 4 * r * 16 * 4;
   int t = (224 * 1024 - tab) / per_team;
   if (t * nw * 32 > 1024) t = 1024 / (nw * 32);
   return t > kMaxTeams ? kMaxTeams : t;
@@ -274,6 +281,9 @@ template <typename T, int OP, int NORM, int VPL, int S, int R, int NW>
 __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
     staged_rows(const Args a, const int team_rt, const int teams) {
   constexpr bool HAS_NORM = (OP != OP_QUANT);
+  constexpr bool MODROW = is_modrow(OP);
+  constexpr bool QOUT = (OP == OP_NORM_MOD_QUANT || OP == OP_NORM_MODROW_QUANT);  // codes + scales out
+  constexpr int NST = MODROW ? 3 : 1;  // rows per ring slot: x (+ scale, shift)
   constexpr bool EXACT = NW > 0;
   extern __shared__ __align__(16) unsigned char smem_raw[];
 
@@ -289,19 +299,19 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
   const float inv_n = 1.f / (float)N;
 
   // ---- fp32 tables -------------------------------------------------------
-  constexpr int NTAB = HAS_NORM ? (NORM == JO_NORM_LAYER ? 4 : 3) : 0;
+  constexpr int NTAB = (HAS_NORM && !MODROW) ? (NORM == JO_NORM_LAYER ? 4 : 3) : 0;
   float* tg = reinterpret_cast<float*>(smem_raw);       // gamma
   float* tsc = tg + N;                                  // 1 + scale
   float* tsh = tsc + N;                                 // shift
   float* tb = tsh + N;                                  // beta (layer norm only)
   uint4* ring = reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) +
-                (size_t)tm * S * R * nvec;
+                (size_t)tm * S * R * NST * nvec;
   // per-team reduction scratch [2 parities][4 slots][R * 16] after all rings
   typedef float RedT[4][R * 16];
   RedT* red = reinterpret_cast<RedT*>(reinterpret_cast<float*>(
-                  reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) + (size_t)teams * S * R * nvec)) +
+                  reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) + (size_t)teams * S * R * NST * nvec)) +
               (size_t)tm * 2;
-  if constexpr (HAS_NORM) {
+  if constexpr (HAS_NORM && !MODROW) {
     const bool has_g = a.gamma != nullptr;
     const bool has_b = NORM == JO_NORM_LAYER && has_g && a.beta != nullptr;
     const T* g = static_cast<const T*>(a.gamma);
@@ -337,10 +347,22 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
         const int64_t row = grp * R + r;
         if (row < M) {
           const char* src = xb + row * rowb;
-          uint4* dst = ring_t + (size_t)(stage * R + r) * nvec;
+          uint4* dst = ring_t + (size_t)((stage * R + r) * NST) * nvec;
 #pragma unroll
           for (int i = 0; i < VPL; ++i)
             if (EXACT || i * team + tl < nvec) cp_async16(dst + i * team, src + i * team * 16);
+          if constexpr (MODROW) {
+            const int64_t mrow = a.mod_group == 1 ? row : row / a.mod_group;
+            const int64_t moff = tl * 16 + mrow * a.mod_stride * (int64_t)sizeof(T);
+            const char* scr = static_cast<const char*>(a.scale) + moff;
+            const char* shr = static_cast<const char*>(a.shift) + moff;
+#pragma unroll
+            for (int i = 0; i < VPL; ++i)
+              if (EXACT || i * team + tl < nvec) {
+                cp_async16(dst + nvec + i * team, scr + i * team * 16);
+                cp_async16(dst + 2 * nvec + i * team, shr + i * team * 16);
+              }
+          }
         }
       }
     }
@@ -361,13 +383,15 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       ok[r] = row0 + r < M;
-      const uint4* src = ring_t + (size_t)(stage * R + r) * nvec;
+      const uint4* src = ring_t + (size_t)((stage * R + r) * NST) * nvec;
 #pragma unroll
       for (int i = 0; i < VPL; ++i)
         // EXACT: rows past M read stale ring data; nothing of them is stored.
         X[r][i].raw = EXACT ? lds16(src + i * team)
                             : (ok[r] && i * team + tl < nvec) ? lds16(src + i * team) : make_uint4(0, 0, 0, 0);
     }
+    const int cur = stage;  // ring slot of this group (modulation rows)
+    (void)cur;
     stage = (stage + 1 == S) ? 0 : stage + 1;
 
     if constexpr (OP == OP_QUANT) {
@@ -441,6 +465,44 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
       uint32_t acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[r] = 0;
+      if constexpr (MODROW) {
+        // Per-row scale / shift from the ring; gamma / beta (16-bit, [N]) from
+        // the L1-cached global copy.  Same expression and grouping as below.
+        const bool has_g = a.gamma != nullptr;
+        const bool has_b = NORM == JO_NORM_LAYER && has_g && a.beta != nullptr;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          if (!(EXACT || i * team + tl < nvec)) continue;
+          const int idx = i * team + tl;
+          const uint4 gv = has_g ? ld_cached(static_cast<const char*>(a.gamma) + idx * 16)
+                                 : make_uint4(MmaType<T>::kOnes, MmaType<T>::kOnes, MmaType<T>::kOnes, MmaType<T>::kOnes);
+          const uint4 bv = has_b ? ld_cached(static_cast<const char*>(a.beta) + idx * 16) : make_uint4(0, 0, 0, 0);
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint4* slot = ring_t + (size_t)((cur * R + r) * NST) * nvec + i * team;
+            const uint4 scv = lds16(slot + nvec), shv = lds16(slot + 2 * nvec);
+            const uint32_t cw[4] = {scv.x, scv.y, scv.z, scv.w}, sw[4] = {shv.x, shv.y, shv.z, shv.w};
+            uint32_t* wr = reinterpret_cast<uint32_t*>(&X[r][i].raw);
+            const float2 rv = make_float2(rr[r], rr[r]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float2 f = unpack2_r<T>(wr[k]);
+              const float2 g2 = unpack2<T>(gw[k]);
+              const float2 c2 = add2(make_float2(1.f, 1.f), unpack2<T>(cw[k]));
+              const float2 s2 = unpack2<T>(sw[k]);
+              if constexpr (NORM == JO_NORM_LAYER) {
+                const float2 nm = make_float2(-mean[r], -mean[r]);
+                f = fma2(fma2(mul2(add2(f, nm), rv), g2, unpack2<T>(bw[k])), c2, s2);
+              } else {
+                f = fma2(mul2(mul2(f, rv), g2), c2, s2);
+              }
+              wr[k] = pack2<T>(f.x, f.y);
+              if constexpr (QOUT) acc[r] = absmax_h2<T>(acc[r], wr[k]);
+            }
+          }
+        }
+      } else
 #pragma unroll
       for (int i = 0; i < VPL; ++i) {
         if (!(EXACT || i * team + tl < nvec)) continue;
@@ -472,14 +534,14 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
             }
             wr[2 * h] = pack2<T>(f0.x, f0.y);      // RNE to T, as the reference's T(float) store
             wr[2 * h + 1] = pack2<T>(f1.x, f1.y);
-            if constexpr (OP == OP_NORM_MOD_QUANT) {
+            if constexpr (QOUT) {
               acc[r] = absmax_h2<T>(acc[r], wr[2 * h]);
               acc[r] = absmax_h2<T>(acc[r], wr[2 * h + 1]);
             }
           }
         }
       }
-      if constexpr (OP == OP_NORM_MOD) {
+      if constexpr (!QOUT) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           if (!ok[r]) continue;
@@ -504,8 +566,10 @@ template <typename T, int OP, int NORM, int VPL, int S, int R, int NW>
 int launch(const Args& a, int team, cudaStream_t st) {
   const int nvec = a.N / 8;
   if (NW > 0 && (team != NW * 32 || nvec != VPL * NW * 32)) return JO_ERR_INVALID;
-  const size_t tab = (OP != OP_QUANT) ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
-  const size_t per_team = (size_t)S * R * nvec * 16 + (size_t)2 * 4 * R * 16 * sizeof(float);
+  constexpr int NST = is_modrow(OP) ? 3 : 1;
+  const size_t tab = (OP != OP_QUANT && !is_modrow(OP))
+                         ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
+  const size_t per_team = (size_t)S * R * NST * nvec * 16 + (size_t)2 * 4 * R * 16 * sizeof(float);
   // Up to 640 threads and ~224 KB of shared memory per CTA, one CTA per SM.
   int teams = NW > 0 ? fixed_teams(OP, NORM, VPL, S, R, NW) : staged_max_threads(VPL, R) / team;
   if (teams > kMaxTeams) teams = kMaxTeams;
@@ -570,6 +634,12 @@ static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream
   using namespace staged;
   const int team = ((nvec + g.vpl - 1) / g.vpl + 31) / 32 * 32;
   if (team > 512) return JO_ERR_INVALID;
+  if constexpr (is_modrow(OP)) {
+    // One row of x, scale and shift per slot, two slots per team.
+    if (fixed_enabled() && g.vpl == 5 && nvec == 640) return launch<T, OP, NORM, 5, 2, 1, 4>(a, team, st);
+    if (fixed_enabled() && g.vpl == 4 && nvec == 640) return launch<T, OP, NORM, 4, 2, 1, 5>(a, team, st);
+    return launch<T, OP, NORM, 4, 2, 1, 0>(a, ((nvec + 3) / 4 + 31) / 32 * 32, st);
+  } else {
   // Fixed geometries for the model's widths: N = 5120 (hidden) and 3072.
   if (g.vpl == 4 && g.r == 2 && g.s == 2 && team * 4 == nvec && fixed_enabled()) {
     if (team == 160) return launch<T, OP, NORM, 4, 2, 2, 5>(a, team, st);
@@ -592,18 +662,20 @@ static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream
   JO_G(20, 1, 2)
 #undef JO_G
   return launch<T, OP, NORM, 4, 2, 2, 0>(a, ((nvec + 3) / 4 + 31) / 32 * 32, st);
+  }
 }
 
 // Entry used by row_ops.cu.  Returns JO_ERR_INVALID (no launch) when the shape
 // is not covered, so the caller falls back to the register kernel.
 int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, const void* gamma, const void* beta,
-                       const void* scale, const void* shift, uint8_t* q, float* s, int64_t M, int N, float eps,
-                       cudaStream_t st) {
+                       const void* scale, const void* shift, int64_t mod_stride, int64_t mod_group, uint8_t* q,
+                       float* s, int64_t M, int N, float eps, cudaStream_t st) {
   using namespace staged;
   if (dtype != JO_DTYPE_BF16 && dtype != JO_DTYPE_F16) return JO_ERR_INVALID;
   const int nvec = N / 8;
   if (N % 8 != 0 || nvec < 128) return JO_ERR_INVALID;
-  Args a{x, y, gamma, beta, scale, shift, q, s, M, N, eps};
+  if (is_modrow(op) && (mod_group < 1 || mod_stride < N)) return JO_ERR_INVALID;
+  Args a{x, y, gamma, beta, scale, shift, q, s, mod_stride, mod_group, M, N, eps};
   const StagedGeom g = pick_geom(nvec);
 #define JO_ST(T)                                                                                          \
   do {                                                                                                    \
@@ -611,6 +683,12 @@ int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, cons
     if (op == OP_NORM_MOD_QUANT)                                                                          \
       return norm == JO_NORM_RMS ? launch_geom<T, OP_NORM_MOD_QUANT, JO_NORM_RMS>(a, nvec, g, st)        \
                                  : launch_geom<T, OP_NORM_MOD_QUANT, JO_NORM_LAYER>(a, nvec, g, st);     \
+    if (op == OP_NORM_MODROW_QUANT)                                                                       \
+      return norm == JO_NORM_RMS ? launch_geom<T, OP_NORM_MODROW_QUANT, JO_NORM_RMS>(a, nvec, g, st)     \
+                                 : launch_geom<T, OP_NORM_MODROW_QUANT, JO_NORM_LAYER>(a, nvec, g, st);  \
+    if (op == OP_NORM_MODROW)                                                                             \
+      return norm == JO_NORM_RMS ? launch_geom<T, OP_NORM_MODROW, JO_NORM_RMS>(a, nvec, g, st)           \
+                                 : launch_geom<T, OP_NORM_MODROW, JO_NORM_LAYER>(a, nvec, g, st);        \
     if (op == OP_NORM_MOD)                                                                                \
       return norm == JO_NORM_RMS ? launch_geom<T, OP_NORM_MOD, JO_NORM_RMS>(a, nvec, g, st)              \
                                  : launch_geom<T, OP_NORM_MOD, JO_NORM_LAYER>(a, nvec, g, st);           \

@@ -89,7 +89,7 @@ def test_quant_rejects_bad_inputs(jo, cuda):
 
 # ------------------------------------------------------- K2 norm+mod -------
 NORM_CASES = [(1, 4, "bf16"), (5, 12, "bf16"), (16, 128, "bf16"), (37, 5120, "bf16"), (8, 1024, "f16"),
-              (9, 512, "f32"), (3, 3072, "bf16"), (4, 13824, "bf16"), (2, 40000, "bf16"), (6, 100, "f32"),
+              (9, 512, "f32"), (3, 3072, "bf16"), (4, 13824, "bf16"), (2, 40000, "bf16"), (6, 100, "f32"), (70, 5120, "f16"),
               (300, 64, "bf16")]
 
 

@@ -3,11 +3,13 @@
 //            :179-208 (host checks).
 //
 // Design (B200): one head vector (D bf16) is owned by D/8 lanes that each move
-// one 16-byte vector, so a warp covers 32*8/D heads and every access is a full
-// 16-byte coalesced load/store.  The same lanes process the q and the k vector
-// of a (token, head) slot, so the per-lane norm weights live in registers and
-// the token's cos/sin entries are fetched once (L1) for both.  Each warp
-// handles U slot groups with all loads issued before any math.
+// one 16-byte vector, so a warp covers 32*8/D heads ("slot group") and every
+// access is a full 16-byte coalesced load/store.  The same lanes process the q
+// and the k vector of a (token, head) slot, so the per-lane norm weights live
+// in registers and the token's cos/sin entries are fetched once for both.
+// The default kernel is persistent (one wave): each warp walks a contiguous
+// run of slot groups with an incremental (token, head) cursor while a per-
+// thread cp.async ring in shared memory keeps the next groups in flight.
 //
 // Numerics: the sum of squares is accumulated and reduced in exactly the
 // reference's order.  The reference gives each of 32 lanes D/32 consecutive
@@ -130,6 +132,207 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   }
 }
 
+// One (token, head) slot's q or k vector of this lane: RMS over the head in
+// the reference's summation order, weight, then the interleaved-pair rotation.
+// wf: this lane's 8 weights (fp32); c2 / s2: this lane's 4 cos / sin entries.
+template <int D, bool ROPE>
+__device__ __forceinline__ uint4 norm_rope_vec(uint4 raw, const float (&wf)[8], uint2 c2, uint2 s2, float eps) {
+  constexpr int LPH = D / 8;
+  constexpr int P = 256 / D;
+  constexpr int EP = 8 / P;
+  Vec16<__nv_bfloat16> v;
+  v.raw = raw;
+  float e[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) e[j] = v.get(j);
+  float part[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < EP; ++j) acc = __fmaf_rn(e[p * EP + j], e[p * EP + j], acc);
+    part[p] = acc;
+  }
+#pragma unroll
+  for (int m = LPH / 2; m > 0; m >>= 1)
+#pragma unroll
+    for (int p = 0; p < P; ++p) part[p] += __shfl_xor_sync(0xffffffffu, part[p], m, 32);
+#pragma unroll
+  for (int m = P / 2; m > 0; m >>= 1)
+#pragma unroll
+    for (int p = 0; p < m; ++p) part[p] = part[p] + part[p + m];
+  const float rms_rcp = rsqrtf(part[0] / static_cast<float>(D) + eps);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) e[j] *= rms_rcp * wf[j];
+  if (!ROPE) {
+#pragma unroll
+    for (int j = 0; j < 8; j += 2)
+      reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(e[j], e[j + 1]));
+    return v.raw;
+  }
+  const __nv_bfloat16* cv = reinterpret_cast<const __nv_bfloat16*>(&c2);
+  const __nv_bfloat16* sv = reinterpret_cast<const __nv_bfloat16*>(&s2);
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const float c = __bfloat162float(cv[j / 2]);
+    const float s = __bfloat162float(sv[j / 2]);
+    const float x1 = e[j], x2 = e[j + 1];
+    const float o0 = x1 * c - x2 * s;
+    const float o1 = x1 * s + x2 * c;
+    reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(o0, o1));
+  }
+  return v.raw;
+}
+
+__device__ __forceinline__ void cpa16(void* smem, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem)), "l"(g)
+               : "memory");
+}
+__device__ __forceinline__ void cpa8(void* smem, const void* g) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((unsigned)__cvta_generic_to_shared(smem)), "l"(g)
+               : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Ring form, persistent: the grid is one wave (blocks per SM x SMs) and every
+// warp owns a contiguous run of slot groups (HPW slots each, so mostly heads
+// of one token), balanced to within one group, which it walks with a cursor
+// (token, head, position in the RoPE table) advanced by HPW heads per group --
+// no division per group.  The groups ahead are staged by each thread into its
+// own shared-memory slots with cp.async (S - 1 groups in flight per thread at
+// no register cost); a thread only reads back the slots it filled itself,
+// after cp.async.wait_group, so no barrier is needed.  Slot layout
+// [stage][q | k | cos,sin][thread]: consecutive threads touch consecutive
+// 16-byte words (conflict-free).  Every lane of a warp runs the same number of
+// iterations (the head reduction shuffles need the full warp); slots past the
+// end are masked.
+template <int D, int S, bool ROPE>
+__global__ void __launch_bounds__(256) qk_norm_rope_ring(
+    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t slots, int seq_len, int num_heads,
+    float eps, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
+    const __nv_bfloat16* __restrict__ cosp, const __nv_bfloat16* __restrict__ sinp, int64_t q_ts, int64_t k_ts) {
+  constexpr int LPH = D / 8;
+  constexpr int HPW = 32 / LPH;
+  __shared__ uint4 ring[S][3][256];
+  const int lane = threadIdx.x & 31;
+  const int hl = lane % LPH;
+  const int t = threadIdx.x;
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+
+  // this warp's groups [g0, g0 + ng): the first `rem` warps take one extra
+  const uint32_t groups = (uint32_t)((slots + HPW - 1) / HPW);
+  const uint32_t base = groups / nwarps, rem = groups % nwarps;
+  const uint32_t g0 = warp * base + (warp < rem ? warp : rem);
+  const int ng = (int)(base + (warp < rem ? 1 : 0));
+  if (ng == 0) return;  // warp-uniform
+
+  float wqf[8], wkf[8];
+  {
+    Vec16<__nv_bfloat16> a, b;
+    a.raw = ld_cached(qw + hl * 8);
+    b.raw = ld_cached(kw + hl * 8);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      wqf[j] = a.get(j);
+      wkf[j] = b.get(j);
+    }
+  }
+
+  struct Cursor {
+    uint32_t slot, tok, head, tr;
+  };
+  Cursor ci;  // issue cursor (runs S - 1 groups ahead)
+  ci.slot = g0 * HPW + lane / LPH;
+  ci.tok = ci.slot / (uint32_t)num_heads;
+  ci.head = ci.slot - ci.tok * (uint32_t)num_heads;
+  ci.tr = ci.tok < (uint32_t)seq_len ? ci.tok : ci.tok % (uint32_t)seq_len;
+  Cursor cc = ci;  // compute cursor
+  auto advance = [&](Cursor& c) {
+    c.slot += HPW;
+    c.head += HPW;
+    while (c.head >= (uint32_t)num_heads) {
+      c.head -= (uint32_t)num_heads;
+      ++c.tok;
+      if (++c.tr == (uint32_t)seq_len) c.tr = 0;
+    }
+  };
+  auto issue = [&](int stage) {
+    if (ci.slot < (uint64_t)slots) {
+      cpa16(&ring[stage][0][t], q + ((int64_t)ci.tok * q_ts + ci.head * D + hl * 8));
+      cpa16(&ring[stage][1][t], k + ((int64_t)ci.tok * k_ts + ci.head * D + hl * 8));
+      if (ROPE) {
+        uint2* cs = reinterpret_cast<uint2*>(&ring[stage][2][t]);
+        cpa8(cs, cosp + (int64_t)ci.tr * (D / 2) + hl * 4);
+        cpa8(cs + 1, sinp + (int64_t)ci.tr * (D / 2) + hl * 4);
+      }
+    }
+    cpa_commit();
+    advance(ci);
+  };
+
+#pragma unroll
+  for (int g = 0; g < S - 1; ++g) {
+    if (g < ng) issue(g);
+    else cpa_commit();  // keep the group count uniform for wait_group
+  }
+  int si = S - 1, sc = 0;  // ring stage of the next issue / of the next compute
+  for (int g = 0; g < ng; ++g) {
+    if (g + S - 1 < ng) issue(si);
+    else cpa_commit();
+    si = si + 1 == S ? 0 : si + 1;
+    cpa_wait<S - 1>();
+    const bool ok = cc.slot < (uint64_t)slots;
+    uint4 vq = make_uint4(0, 0, 0, 0), vk = vq;
+    uint2 c2 = make_uint2(0, 0), s2 = c2;
+    if (ok) {
+      vq = ring[sc][0][t];
+      vk = ring[sc][1][t];
+      if (ROPE) {
+        const uint4 cs = ring[sc][2][t];
+        c2 = make_uint2(cs.x, cs.y);
+        s2 = make_uint2(cs.z, cs.w);
+      }
+    }
+    sc = sc + 1 == S ? 0 : sc + 1;
+    const uint4 oq = norm_rope_vec<D, ROPE>(vq, wqf, c2, s2, eps);
+    const uint4 okv = norm_rope_vec<D, ROPE>(vk, wkf, c2, s2, eps);
+    if (ok) {
+      st_stream(q + ((int64_t)cc.tok * q_ts + cc.head * D + hl * 8), oq);
+      st_stream(k + ((int64_t)cc.tok * k_ts + cc.head * D + hl * 8), okv);
+    }
+    advance(cc);
+  }
+  cpa_wait<0>();
+}
+
+template <int D, int S>
+int launch_ring(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw,
+                const void* kw, const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
+  constexpr int HPW = 32 / (D / 8);
+  auto* qp = static_cast<__nv_bfloat16*>(q);
+  auto* kp = static_cast<__nv_bfloat16*>(k);
+  auto* qwp = static_cast<const __nv_bfloat16*>(qw);
+  auto* kwp = static_cast<const __nv_bfloat16*>(kw);
+  auto* cp = static_cast<const __nv_bfloat16*>(c);
+  auto* sp = static_cast<const __nv_bfloat16*>(s);
+  auto kern = c ? qk_norm_rope_ring<D, S, true> : qk_norm_rope_ring<D, S, false>;
+  static int per_sm[2] = {0, 0};
+  int& bps = per_sm[c ? 1 : 0];
+  if (bps == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kern, 256, 0) != cudaSuccess || bps < 1))
+    bps = 1;
+  const int64_t groups = (slots + HPW - 1) / HPW;
+  const int64_t need = (groups + 7) / 8;  // one group per warp at least
+  const int64_t wave = (int64_t)bps * sm_count();
+  const int64_t blocks = need < wave ? need : wave;
+  kern<<<(unsigned)blocks, 256, 0, st>>>(qp, kp, slots, seq_len, num_heads, eps, qwp, kwp, cp, sp, q_ts, k_ts);
+  return check_launch("fused_qk_norm_rope_3d_paired");
+}
+
 template <int D, int U>
 int launch_u(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
              const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
@@ -151,29 +354,23 @@ int launch_u(void* q, void* k, int64_t slots, int seq_len, int num_heads, float 
   return check_launch("fused_qk_norm_rope_3d_paired");
 }
 
-// Slot groups per warp (loads in flight per lane = 2 * U).  U = 1 measured
-// fastest on B200 (more CTAs in flight beat deeper per-warp batches);
-// JO_QKR_U overrides for measurements.
-static int qkr_u() {
-  static int u = -1;
-  if (u < 0) {
-    const char* e = getenv("JO_QKR_U");
-    u = e ? atoi(e) : 1;
-    if (u != 1 && u != 2 && u != 4 && u != 8) u = 1;
-  }
-  return u;
+// Kernel choice for measurements: JO_QKR_U=1/2 selects the one-shot kernel
+// (one slot group per warp, U groups), JO_QKR_S=2/4 the ring depth of the
+// persistent ring kernel (default, 3 stages).
+static int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : dflt;
 }
 
 template <int D>
 int launch(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
            const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
-  switch (qkr_u()) {
-    case 1: return launch_u<D, 1>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-    case 4: return launch_u<D, 4>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-    case 8: return launch_u<D, 8>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-    case 2: return launch_u<D, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-    default: return launch_u<D, 1>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-  }
+  static const int u = env_int("JO_QKR_U", 0), ring = env_int("JO_QKR_S", 3);
+  if (u == 1) return launch_u<D, 1>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  if (u == 2) return launch_u<D, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  if (ring == 2) return launch_ring<D, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  if (ring == 4) return launch_ring<D, 4>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  return launch_ring<D, 3>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
 }
 
 }  // namespace

@@ -167,7 +167,10 @@ def test_rmsnorm(jo, cuda, M, N, dtype):
 
 # -------------------------------------------------------- K1 qk-rope -------
 @pytest.mark.parametrize("B,grid,H,D", [(1, (2, 4, 8), 8, 128), (2, (1, 3, 5), 3, 64), (1, (1, 2, 9), 2, 256),
-                                        (1, (1, 1, 1), 1, 128), (3, (1, 1, 7), 5, 128)])
+                                        (1, (1, 1, 1), 1, 128), (3, (1, 1, 7), 5, 128),
+                                        # several slot groups per warp of the persistent kernel, with a
+                                        # remainder; heads per token below the heads per group (3 < 4)
+                                        (1, (4, 16, 32), 40, 128), (2, (4, 32, 64), 3, 64)])
 def test_qk_norm_rope(jo, cuda, B, grid, H, D):
     rng = np.random.default_rng(B * 100 + H + D)
     L = grid[0] * grid[1] * grid[2]

@@ -134,9 +134,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 
 // One (token, head) slot's q or k vector of this lane: RMS over the head in
 // the reference's summation order, weight, then the interleaved-pair rotation.
-// wf: this lane's 8 weights (fp32); c2 / s2: this lane's 4 cos / sin entries.
+// wf: this lane's 8 weights (fp32); cf / sf: this lane's 4 cos / sin entries
+// (fp32, shared by the q and the k vector of the slot).
 template <int D, bool ROPE>
-__device__ __forceinline__ uint4 norm_rope_vec(uint4 raw, const float (&wf)[8], uint2 c2, uint2 s2, float eps) {
+__device__ __forceinline__ uint4 norm_rope_vec(uint4 raw, const float (&wf)[8], const float (&cf)[4],
+                                               const float (&sf)[4], float eps) {
   constexpr int LPH = D / 8;
   constexpr int P = 256 / D;
   constexpr int EP = 8 / P;
@@ -170,18 +172,22 @@ __device__ __forceinline__ uint4 norm_rope_vec(uint4 raw, const float (&wf)[8], 
       reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(e[j], e[j + 1]));
     return v.raw;
   }
-  const __nv_bfloat16* cv = reinterpret_cast<const __nv_bfloat16*>(&c2);
-  const __nv_bfloat16* sv = reinterpret_cast<const __nv_bfloat16*>(&s2);
 #pragma unroll
   for (int j = 0; j < 8; j += 2) {
-    const float c = __bfloat162float(cv[j / 2]);
-    const float s = __bfloat162float(sv[j / 2]);
+    const float c = cf[j / 2];
+    const float s = sf[j / 2];
     const float x1 = e[j], x2 = e[j + 1];
     const float o0 = x1 * c - x2 * s;
     const float o1 = x1 * s + x2 * c;
     reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(o0, o1));
   }
   return v.raw;
+}
+__device__ __forceinline__ void unpack_cs(uint2 c2, uint2 s2, float (&cf)[4], float (&sf)[4]) {
+  const float2 c01 = unpack2<__nv_bfloat16>(c2.x), c23 = unpack2<__nv_bfloat16>(c2.y);
+  const float2 s01 = unpack2<__nv_bfloat16>(s2.x), s23 = unpack2<__nv_bfloat16>(s2.y);
+  cf[0] = c01.x; cf[1] = c01.y; cf[2] = c23.x; cf[3] = c23.y;
+  sf[0] = s01.x; sf[1] = s01.y; sf[2] = s23.x; sf[3] = s23.y;
 }
 
 __device__ __forceinline__ void cpa16(void* smem, const void* g) {
@@ -299,8 +305,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_ring(
       }
     }
     sc = sc + 1 == S ? 0 : sc + 1;
-    const uint4 oq = norm_rope_vec<D, ROPE>(vq, wqf, c2, s2, eps);
-    const uint4 okv = norm_rope_vec<D, ROPE>(vk, wkf, c2, s2, eps);
+    float cf[4], sf[4];
+    unpack_cs(c2, s2, cf, sf);
+    const uint4 oq = norm_rope_vec<D, ROPE>(vq, wqf, cf, sf, eps);
+    const uint4 okv = norm_rope_vec<D, ROPE>(vk, wkf, cf, sf, eps);
     if (ok) {
       st_stream(q + ((int64_t)cc.tok * q_ts + cc.head * D + hl * 8), oq);
       st_stream(k + ((int64_t)cc.tok * k_ts + cc.head * D + hl * 8), okv);

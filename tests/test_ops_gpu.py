@@ -90,6 +90,7 @@ def test_quant_rejects_bad_inputs(jo, cuda):
 # ------------------------------------------------------- K2 norm+mod -------
 NORM_CASES = [(1, 4, "bf16"), (5, 12, "bf16"), (16, 128, "bf16"), (37, 5120, "bf16"), (8, 1024, "f16"),
               (9, 512, "f32"), (3, 3072, "bf16"), (4, 13824, "bf16"), (2, 40000, "bf16"), (6, 100, "f32"), (70, 5120, "f16"),
+              (1601, 5120, "bf16"),
               (300, 64, "bf16")]
 
 
@@ -284,12 +285,25 @@ def test_qk_norm_rope_strided_matches_dense(jo, cuda, rope):
     assert torch.equal(qkv[:, 2], v0)
 
 
-@pytest.mark.parametrize("M,N", [(37, 1024), (130, 5120), (9, 2048), (3, 13824)])
+@pytest.mark.parametrize("M,N", [(37, 1024), (130, 5120), (9, 2048), (3, 13824), (41, 3072)])
 @pytest.mark.parametrize("nt", [0, 1])
 @pytest.mark.parametrize("affine", [False, True])
 def test_broadcast_modulation_paths(jo, cuda, M, N, nt, affine):
     """[N] shift/scale (the model's adaLN layout): fused norm->quant and
     norm->modulate through the staged kernel, against the oracle."""
+    _check_broadcast(jo, cuda, M, N, nt, affine)
+
+
+@pytest.mark.parametrize("M,N,nt,affine", [(2501, 5120, 1, True), (2501, 5120, 0, False), (2001, 3072, 1, True),
+                                            (2001, 3072, 0, True)])
+def test_broadcast_modulation_many_groups(jo, cuda, M, N, nt, affine):
+    """Enough rows that every team of the persistent staged kernel walks
+    several row groups through its ring (and an odd row count leaves a
+    half-filled last group)."""
+    _check_broadcast(jo, cuda, M, N, nt, affine)
+
+
+def _check_broadcast(jo, cuda, M, N, nt, affine):
     rng = np.random.default_rng(M + N + nt * 3 + affine)
     x = outlier_activations(rng, M, N)
     sc, sh = randn(rng, (N,), 0.1), randn(rng, (N,), 0.1)

@@ -155,6 +155,35 @@ int jo_fp8_scaled_mm_ex(const void* mat_a, const void* mat_b, const float* scale
  * reset != 0 clears it.  Synchronous; for tests. */
 int jo_gemm_last_fault(int reset);
 
+/*
+ * Sequence-parallel exchange fused into the FP8 GEMM (no reference
+ * counterpart: the reference runs the denoiser on one GPU).  Computes the
+ * jo_fp8_scaled_mm result [M, N] with N = parts * ranks * heads_per_rank *
+ * head_dim (parts = q, k, v) and, instead of writing it row-major, stores
+ * row m of head h of part p into dst[p * ranks + h / heads_per_rank] at token
+ * tok0 + m, local head h % heads_per_rank of a [tokens, heads_per_rank,
+ * head_dim] buffer: the all-to-all that turns a token shard into a head shard
+ * (replaces torch.distributed.all_to_all_single after the QKV projection).
+ * Destinations of other ranks are peer pointers from jo_ipc_open.  The caller
+ * synchronises the ranks (e.g. a one-element collective on the same stream)
+ * before any rank reads its buffers.
+ */
+int jo_fp8_scaled_mm_scatter(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                             const void* bias, int64_t M, int64_t N, int64_t K, int out_dtype,
+                             const void* const* dst, int parts, int ranks, int heads_per_rank, int head_dim,
+                             int64_t tok0, void* stream);
+
+/*
+ * Peer-memory plumbing (legacy CUDA IPC, no multicast objects) for the
+ * exchange above.  jo_ipc_get_handle writes the 64-byte handle of the
+ * allocation holding dev_ptr and the byte offset of dev_ptr in it;
+ * jo_ipc_open maps another process's handle on the current device;
+ * jo_ipc_close unmaps it.
+ */
+int jo_ipc_get_handle(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int jo_ipc_open(const void* handle, void** base_out);
+int jo_ipc_close(void* base);
+
 #ifdef __cplusplus
 }
 #endif

@@ -155,7 +155,27 @@ struct Params {
   const void* resid;  // JO_EPI_RESID_GATE: residual [M, N] (may alias d)
   const void* gate;   // JO_EPI_RESID_GATE: gate [N]
   int group;          // 2-SM kernel: pair-tile rows per rasterisation group
+  // Head-scatter output (jo_fp8_scaled_mm_scatter): output column n is part
+  // n / sc_width (q, k, v) of head h = (n % sc_width) / sc_dh, owned by rank
+  // h / sc_hpr; row m goes to token sc_tok0 + m of that rank's
+  // [tokens, sc_hpr, sc_dh] buffer sc_dst[part * 8 + rank] (a peer's memory
+  // for other ranks: plain 16-byte stores over NVLink).
+  int scatter;
+  int sc_width, sc_dh, sc_hpr;
+  int64_t sc_tok0;
+  void* sc_dst[24];
 };
+
+template <typename OutT>
+__device__ __forceinline__ OutT* scatter_dst(const Params& p, int m, int n0) {
+  const int part = n0 / p.sc_width;
+  const int col = n0 - part * p.sc_width;
+  const int h = col / p.sc_dh;
+  const int d = h / p.sc_hpr;
+  const int hl = h - d * p.sc_hpr;
+  OutT* base = static_cast<OutT*>(p.sc_dst[part * 8 + d]);
+  return base + ((p.sc_tok0 + m) * p.sc_hpr + hl) * (int64_t)p.sc_dh + (col - h * p.sc_dh);
+}
 
 // Epilogue of one 32-column chunk of one output row (one thread = one row):
 //   o = out(fma(sa, sb[n] * acc, bias[n]))  or  out(sa * (sb[n] * acc))
@@ -166,7 +186,7 @@ struct Params {
 // sgl_fused_ops.py:114-117, applied to the rounded GEMM output.)
 template <typename OutT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Params& p, int m, float sa, int n0,
-                                               OutT* drow) {
+                                               OutT* dst) {
   const OutT* bias = static_cast<const OutT*>(p.bias);
   const bool full = n0 + 32 <= p.N;
   float y[32];
@@ -212,13 +232,13 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Pa
     uint32_t w[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) w[j] = pack2<OutT>(y[2 * j], y[2 * j + 1]);
-    uint4* dst = reinterpret_cast<uint4*>(drow + n0);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    for (int j = 0; j < 4; ++j) d4[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (n0 + j < p.N) drow[n0 + j] = from_f32<OutT>(y[j]);
+      if (n0 + j < p.N) dst[j] = from_f32<OutT>(y[j]);
   }
 }
 
@@ -369,13 +389,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_wait_ld();
         const int n0 = nb * BN + c;
         if (!mok || n0 >= p.N) continue;
-        epilogue_chunk<OutT>(r, p, m, sa, n0, drow);
+        epilogue_chunk<OutT>(r, p, m, sa, n0, p.scatter ? scatter_dst<OutT>(p, m, n0) : drow + n0);
       }
       // hand the accumulator back to the MMA warp
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
     }
+    if (p.scatter) __threadfence_system();  // head-scatter: peer stores visible system-wide
   }
 
   fence_before();
@@ -617,12 +638,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         tmem_wait_ld();
         const int n0 = nb * BN + c;
         if (!mok || n0 >= p.N) continue;
-        epilogue_chunk<OutT>(r, p, m, sa, n0, drow);
+        epilogue_chunk<OutT>(r, p, m, sa, n0, p.scatter ? scatter_dst<OutT>(p, m, n0) : drow + n0);
       }
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(ltempty0 + 8 * buf);
     }
+    if (p.scatter) __threadfence_system();  // head-scatter: peer stores visible system-wide
   }
 
   fence_before();
@@ -724,9 +746,16 @@ int launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, Params p, cudaStrea
   return check_launch("fp8_scaled_mm");
 }
 
+struct ScatterSpec {
+  int width, dh, hpr;
+  int64_t tok0;
+  void* dst[24];
+};
+
 template <typename OutT>
 int launch(const void* A, const void* B, const float* sa, const float* sb, const void* bias, void* D, int64_t M,
-           int64_t N, int64_t K, int epi, const void* resid, const void* gate, cudaStream_t st) {
+           int64_t N, int64_t K, int epi, const void* resid, const void* gate, cudaStream_t st,
+           const ScatterSpec* sc = nullptr) {
   CUtensorMap ta, tb;
   const bool pair = M > 128 && use_2sm();
   if (!make_map(&ta, A, M, K, BM) || !make_map(&tb, B, N, K, pair ? 128 : BN)) {
@@ -748,6 +777,12 @@ int launch(const void* A, const void* B, const float* sa, const float* sb, const
   p.epilogue = epi;
   p.resid = resid;
   p.gate = gate;
+  p.scatter = sc != nullptr;
+  p.sc_width = sc ? sc->width : 0;
+  p.sc_dh = sc ? sc->dh : 0;
+  p.sc_hpr = sc ? sc->hpr : 0;
+  p.sc_tok0 = sc ? sc->tok0 : 0;
+  for (int i = 0; i < 24; ++i) p.sc_dst[i] = sc ? sc->dst[i] : nullptr;
   if (pair) return launch_2sm<OutT>(ta, tb, p, st);
   const int smem = STAGES * STAGE_BYTES + 1024 + 256;
   static bool attr = false;
@@ -807,6 +842,56 @@ int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a
   }
   return jo_fp8_scaled_mm_ex(mat_a, mat_b, scales_a, scales_b, bias, out, M, N, K, out_dtype, epilogue, nullptr,
                              nullptr, stream);
+}
+
+// FP8 GEMM whose epilogue scatters each (row, head) of the [M, parts*ranks*
+// heads_per_rank*head_dim] result to the rank that owns the head (the
+// sequence-parallel all-to-all fused into the GEMM).  dst[part * ranks + r] is
+// rank r's [tokens, heads_per_rank, head_dim] buffer for part `part` (a peer
+// pointer for r != this rank, opened with jo_ipc_open); row m lands at token
+// tok0 + m.  Stores only (no TMA, no multicast); each epilogue thread ends
+// with a system-scope fence, and the caller orders the consumers after a
+// cross-rank synchronisation.
+int jo_fp8_scaled_mm_scatter(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
+                             const void* bias, int64_t M, int64_t N, int64_t K, int out_dtype,
+                             const void* const* dst, int parts, int ranks, int heads_per_rank, int head_dim,
+                             int64_t tok0, void* stream) {
+  using namespace jo;
+  const char* what = "fp8_scaled_mm_scatter";
+  JO_REQUIRE(out_dtype == JO_DTYPE_BF16 || out_dtype == JO_DTYPE_F16, JO_ERR_DTYPE,
+             "out_dtype must be Half or BFloat16");
+  JO_REQUIRE(parts >= 1 && parts <= 3 && ranks >= 1 && ranks <= 8 && heads_per_rank >= 1 && head_dim >= 32 &&
+                 head_dim % 32 == 0 && tok0 >= 0,
+             JO_ERR_INVALID, "%s: parts 1..3, ranks 1..8, head_dim a multiple of 32, tok0 >= 0", what);
+  JO_REQUIRE(N == (int64_t)parts * ranks * heads_per_rank * head_dim, JO_ERR_INVALID,
+             "%s: N (%lld) must equal parts * ranks * heads_per_rank * head_dim", what, (long long)N);
+  JO_REQUIRE(M >= 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && K % 16 == 0,
+             JO_ERR_INVALID, "%s: invalid shape", what);
+  JO_REQUIRE(M == 0 || (mat_a && mat_b && scales_a && scales_b && dst), JO_ERR_INVALID, "%s: null pointer", what);
+  JO_REQUIRE(aligned16(mat_a) && aligned16(mat_b) && aligned16(scales_b) && (!bias || aligned8(bias)),
+             JO_ERR_ALIGN, "%s: operands must be 16-byte aligned (bias 8-byte)", what);
+  gemm::ScatterSpec sc;
+  sc.width = ranks * heads_per_rank * head_dim;
+  sc.dh = head_dim;
+  sc.hpr = heads_per_rank;
+  sc.tok0 = tok0;
+  for (int i = 0; i < 24; ++i) sc.dst[i] = nullptr;
+  for (int part = 0; part < parts; ++part)
+    for (int r = 0; r < ranks; ++r) {
+      void* d = const_cast<void*>(dst[part * ranks + r]);
+      JO_REQUIRE(d && aligned16(d), JO_ERR_ALIGN, "%s: destination %d of part %d is null or not 16-byte aligned",
+                 what, r, part);
+      sc.dst[part * 8 + r] = d;
+    }
+  int st = require_sm100();
+  if (st != JO_OK) return st;
+  if (M == 0) return JO_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return out_dtype == JO_DTYPE_BF16
+             ? gemm::launch<__nv_bfloat16>(mat_a, mat_b, scales_a, scales_b, bias, sc.dst[0], M, N, K, JO_EPI_NONE,
+                                           nullptr, nullptr, s, &sc)
+             : gemm::launch<__half>(mat_a, mat_b, scales_a, scales_b, bias, sc.dst[0], M, N, K, JO_EPI_NONE, nullptr,
+                                    nullptr, s, &sc);
 }
 
 // Fault code of the GEMM kernel's bounded waits (0 = none) and reset.  Reads

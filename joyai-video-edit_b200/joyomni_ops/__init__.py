@@ -19,6 +19,8 @@ from __future__ import annotations
 
 from typing import Optional
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -365,6 +367,32 @@ def fp8_scaled_mm_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, re
     in the GEMM epilogue.  out may be the residual itself (in place)."""
     return _fp8_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, _lib.JO_EPI_RESID_GATE, out=out,
                    residual=residual, gate=gate)
+
+
+def fp8_scaled_mm_scatter(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, dst_ptrs, parts, ranks,
+                          heads_per_rank, head_dim, tok0):
+    """fp8_scaled_mm whose epilogue scatters the [M, parts*ranks*heads_per_rank*
+    head_dim] result by head: row m, head h of part p goes to token tok0 + m,
+    local head h % heads_per_rank of the [tokens, heads_per_rank, head_dim]
+    buffer at dst_ptrs[p * ranks + h // heads_per_rank] (device addresses; a
+    peer rank's buffer through joyomni_stack.peer).  The sequence-parallel
+    all-to-all after the QKV projection, fused into the GEMM (new entry)."""
+    if not has_fp8():
+        raise NotImplementedError("joyomni_b200 was built without the FP8 GEMM")
+    _fp8_mm_checks(mat_a, mat_b, scales_a, scales_b, out_dtype, bias)
+    M, K = mat_a.shape
+    N = mat_b.size(1)
+    _chk(len(dst_ptrs) == parts * ranks, "dst_ptrs must hold parts * ranks addresses")
+    _chk(N == parts * ranks * heads_per_rank * head_dim, "N must equal parts * ranks * heads_per_rank * head_dim")
+    lda = mat_a.stride(0) if M > 1 else K
+    ldb = mat_b.stride(1) if N > 1 else K
+    _chk(lda == K and ldb == K, "mat_a rows and mat_b columns must be densely packed")
+    arr = (ctypes.c_void_p * len(dst_ptrs))(*[int(p) for p in dst_ptrs])
+    with _Device(mat_a) as st:
+        _check(_L.jo_fp8_scaled_mm_scatter(
+            mat_a.data_ptr(), mat_b.data_ptr(), scales_a.data_ptr(), scales_b.data_ptr(),
+            bias.data_ptr() if bias is not None else None, M, N, K, _DT[out_dtype], arr, parts, ranks,
+            heads_per_rank, head_dim, tok0, st))
 
 
 from . import _torch_ops  # noqa: E402,F401  (registers torch.ops.joyomni_ops.*)

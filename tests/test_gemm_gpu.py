@@ -138,3 +138,44 @@ def test_fp8_scaled_mm_out_row_slice(jo, cuda):
                      out=big[50:250])
     assert torch.equal(big[50:250], ref)
     assert (big[:50] == 7).all() and (big[250:] == 7).all()
+
+
+@pytest.mark.parametrize("M,ranks,hpr,dh,tok0", [(300, 4, 2, 128, 7), (100, 2, 3, 64, 0), (513, 8, 1, 128, 40)])
+def test_fp8_scaled_mm_scatter_emulated_ranks(jo, cuda, M, ranks, hpr, dh, tok0):
+    """The head-scatter epilogue on one GPU, with the `ranks` destinations as
+    local buffers: every (row, head) lands where the sequence-parallel
+    all-to-all would put it, bit-identical to the plain GEMM's value, and
+    nothing outside the written token rows is touched."""
+    rng = np.random.default_rng(M + ranks + dh)
+    parts, K = 3, 256
+    N = parts * ranks * hpr * dh
+    a, sa, b, sb = _operands(rng, M, N, K)
+    bias = randn(rng, (N,), 0.01)
+    ref = _run(jo, cuda, a, sa, b, sb, bias)
+    A = torch.from_numpy(a).to(cuda).view(torch.float8_e4m3fn)
+    B = torch.from_numpy(b).to(cuda).view(torch.float8_e4m3fn).t()
+    T = tok0 + M + 3
+    sentinel = torch.tensor(-7.0, dtype=torch.bfloat16)
+    dst = [torch.full((T, hpr, dh), -7.0, dtype=torch.bfloat16, device=cuda) for _ in range(parts * ranks)]
+    jo.fp8_scaled_mm_scatter(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), torch.bfloat16,
+                             torch.from_numpy(bias).to(torch.bfloat16).to(cuda), [d.data_ptr() for d in dst],
+                             parts, ranks, hpr, dh, tok0)
+    torch.cuda.synchronize()
+    want = ref.view(M, parts, ranks, hpr, dh)
+    for p in range(parts):
+        for r in range(ranks):
+            got = dst[p * ranks + r]
+            assert torch.equal(got[tok0:tok0 + M], want[:, p, r])
+            assert bool((got[:tok0] == sentinel.to(cuda)).all()) and bool((got[tok0 + M:] == sentinel.to(cuda)).all())
+
+
+def test_fp8_scaled_mm_scatter_rejects_bad_layout(jo, cuda):
+    a = torch.zeros((4, 64), dtype=torch.float8_e4m3fn, device=cuda)
+    b = torch.zeros((96, 64), dtype=torch.float8_e4m3fn, device=cuda).t()
+    sa = torch.ones(4, device=cuda)
+    sb = torch.ones(96, device=cuda)
+    d = torch.empty((4, 1, 32), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(RuntimeError):
+        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 3, 3, 1, 2, 32, 0)
+    with pytest.raises(RuntimeError):
+        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 2, 3, 1, 1, 32, 0)

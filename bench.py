@@ -383,7 +383,11 @@ def stack_bench(torch, dev, world):
            **({} if graph else {"capture_error": getattr(st, "capture_error", "")}),
            "fps": round(24 / (chunk_ms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
            "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
-           "attention": "torch SDPA (cuDNN/flash), bf16"}
+           "attention": "torch SDPA (cuDNN/flash), bf16",
+           "sp_exchange": ("none (P = 1)" if world == 1 else
+                           "q/k/v scattered by head in the QKV GEMM epilogue (peer stores over NVLink)"
+                           if st.region is not None else "NCCL all_to_all")}
+    st.close()
     del st
     torch.cuda.empty_cache()
     return out

@@ -26,6 +26,7 @@ ulysses.py) is new; with P = 1 it degenerates to plain single-GPU execution.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import List, Optional
 
@@ -34,7 +35,7 @@ import torch.nn.functional as F
 
 import joyomni_ops as jo
 
-from .ulysses import SeqParallel
+from .ulysses import SeqParallel, shard_range, split_sizes
 
 NORM_EPS = 1e-6
 FP8 = torch.float8_e4m3fn
@@ -96,6 +97,12 @@ class Fp8Weight:
         f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
         return f(xq, self.t, xs, self.scale, torch.bfloat16, self.b, out=out)
 
+    def scatter(self, xq, xs, dst_ptrs, ranks, heads_per_rank, head_dim, tok0):
+        """QKV projection with the sequence-parallel all-to-all in its epilogue:
+        every (token, head) is stored in the owning rank's q / k / v buffer."""
+        jo.fp8_scaled_mm_scatter(xq, self.t, xs, self.scale, torch.bfloat16, self.b, dst_ptrs, 3, ranks,
+                                 heads_per_rank, head_dim, tok0)
+
     def residual(self, xq, xs, res, gate, out=None):
         """res + gate * (x @ W + b), gated residual fused in the GEMM epilogue."""
         return jo.fp8_scaled_mm_residual(xq, self.t, xs, self.scale, torch.bfloat16, self.b, res, gate, out=out)
@@ -134,11 +141,13 @@ class LayerKV:
     tokens, so the all-to-all writes the current chunk's keys straight into the
     buffer and the attention keys are one contiguous prefix."""
 
-    def __init__(self, cfg: StackConfig, sp: SeqParallel, device):
+    def __init__(self, cfg: StackConfig, sp: SeqParallel, device, k=None, v=None):
         self.cap = cfg.cache_chunks * cfg.img_tokens
         n = sp.total_len + self.cap
-        self.k = torch.empty((n, sp.local_heads, cfg.head_dim), dtype=torch.bfloat16, device=device)
-        self.v = torch.empty_like(self.k)
+        self.k = k if k is not None else torch.empty((n, sp.local_heads, cfg.head_dim), dtype=torch.bfloat16,
+                                                     device=device)
+        self.v = v if v is not None else torch.empty_like(self.k)
+        self.peer = None        # PeerExchange of the layer (P > 1, peer mode)
         self.valid = 0          # cached image tokens
         self.next_slot = 0
         self.cur = sp.total_len
@@ -168,6 +177,20 @@ class LayerKV:
         self.next_slot = chunks % (self.cap // self.img_len)
 
 
+@dataclass
+class PeerExchange:
+    """Per-layer view of the peer exchange: the head-sharded q buffer, the
+    gathered-order segments (offset, image rows, text rows, first image token)
+    of every rank, the full RoPE tables, and the 3 x P destination addresses
+    (q, k, v of every rank) handed to the scattering QKV projection."""
+    region: object
+    q: torch.Tensor
+    seg: list
+    cos: torch.Tensor
+    sin: torch.Tensor
+    dst: list
+
+
 class Block:
     def __init__(self, cfg: StackConfig, gen, device):
         self.cfg = cfg
@@ -180,6 +203,9 @@ class Block:
         Li, Lt = img.shape[0], txt.shape[0]
         im = (self.img.mod + vec).unbind(0)
         tm = (self.txt.mod + vec).unbind(0)
+
+        if sp.world > 1 and kv.peer is not None:
+            return self._forward_peer(img, txt, im, tm, kv, sp)
 
         # ---- QKV of both streams into one [L_local, 3, H, Dh] buffer --------
         qkv = torch.empty((Li + Lt, 3 * D), dtype=torch.bfloat16, device=img.device)
@@ -208,6 +234,38 @@ class Block:
         txt = self._tail(self.txt, tm, txt, o[Li:])
         return img, txt
 
+    def _forward_peer(self, img, txt, im, tm, kv: "LayerKV", sp: SeqParallel):
+        """P > 1 with the exchange fused into the QKV projection: the epilogue
+        scatters q, k, v by head into the owning ranks' buffers (peer memory),
+        then every rank normalises / rotates its heads of all tokens, one
+        launch per rank segment of the gathered token order."""
+        cfg = self.cfg
+        Dh, D = cfg.head_dim, cfg.hidden
+        Li = img.shape[0]
+        ex = kv.peer
+        xq, xs = norm_mod_quant(img, im[0], im[1])
+        self.img.qkv.scatter(xq, xs, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0])
+        tq, ts = norm_mod_quant(txt, tm[0], tm[1])
+        self.txt.qkv.scatter(tq, ts, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0] + Li)
+        ex.region.sync()
+        q = ex.q
+        for off, ni, nt, i0 in ex.seg:
+            jo.qk_norm_rope_strided(q[off:off + ni][None], kv.k[off:off + ni][None], NORM_EPS, self.img.q_norm,
+                                    self.img.k_norm, ex.cos[i0:i0 + ni], ex.sin[i0:i0 + ni])
+            if nt:
+                jo.qk_norm_rope_strided(q[off + ni:off + ni + nt][None], kv.k[off + ni:off + ni + nt][None],
+                                        NORM_EPS, self.txt.q_norm, self.txt.k_norm)
+        k_all, v_all = kv.keys()
+        with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
+                                             torch.nn.attention.SDPBackend.FLASH_ATTENTION,
+                                             torch.nn.attention.SDPBackend.EFFICIENT_ATTENTION]):
+            o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k_all.permute(1, 0, 2)[None],
+                                               v_all.permute(1, 0, 2)[None])
+        o = sp.heads_to_seq(o[0].permute(1, 0, 2)).reshape(Li + txt.shape[0], D)
+        img = self._tail(self.img, im, img, o[:Li])
+        txt = self._tail(self.txt, tm, txt, o[Li:])
+        return img, txt
+
     @staticmethod
     def _tail(st: Stream, m, x, attn):
         aq, as_ = quant(attn)
@@ -228,10 +286,16 @@ class Stack:
         gen = torch.Generator(device=device).manual_seed(cfg.seed)
         n = cfg.layers if layers is None else layers
         self.blocks: List[Block] = [Block(cfg, gen, device) for _ in range(n)]
-        self.kv = [LayerKV(cfg, self.sp, device) for _ in range(n)]
         cos, sin = rope_tables(cfg, device)
         a, b = self.sp.img_range
         self.cos, self.sin = cos[a:b].contiguous(), sin[a:b].contiguous()
+        self.region = None
+        # P > 1: the QKV projections scatter into the owning ranks' buffers over
+        # peer memory (JOYOMNI_SP_EXCHANGE=nccl selects the NCCL all-to-all path).
+        if self.sp.world > 1 and os.environ.get("JOYOMNI_SP_EXCHANGE", "peer") == "peer":
+            self.kv = self._peer_kv(n, cos, sin, device)
+        else:
+            self.kv = [LayerKV(cfg, self.sp, device) for _ in range(n)]
 
     def forward(self, img, txt, vec):
         for blk, kv in zip(self.blocks, self.kv):
@@ -241,6 +305,40 @@ class Stack:
     def commit_kv(self):
         for kv in self.kv:
             kv.commit(self.sp)
+        if self.region is not None:
+            # the next chunk's scatters must not overtake a slower rank's commit copies
+            self.region.sync()
+
+    def _peer_kv(self, n: int, cos, sin, device) -> List["LayerKV"]:
+        from .peer import PeerRegion, RegionLayout
+        cfg, sp = self.cfg, self.sp
+        hpr, Dh = sp.local_heads, cfg.head_dim
+        rows = sp.total_len + cfg.cache_chunks * cfg.img_tokens
+        lay = RegionLayout()
+        lay.add("q", (sp.total_len, hpr, Dh))
+        for i in range(n):
+            lay.add(f"k{i}", (rows, hpr, Dh))
+            lay.add(f"v{i}", (rows, hpr, Dh))
+        self.region = PeerRegion(lay, sp.group, sp.world, sp.rank, device)
+        isz, tsz = split_sizes(cfg.img_tokens, sp.world), split_sizes(cfg.txt_tokens, sp.world)
+        seg, off = [], 0
+        for r in range(sp.world):
+            seg.append((off, isz[r], tsz[r], shard_range(cfg.img_tokens, sp.world, r)[0]))
+            off += isz[r] + tsz[r]
+        q = self.region.tensor("q")
+        kvs = []
+        for i in range(n):
+            kv = LayerKV(cfg, sp, device, k=self.region.tensor(f"k{i}"), v=self.region.tensor(f"v{i}"))
+            kv.peer = PeerExchange(self.region, q, seg, cos, sin,
+                                   [self.region.ptr(r, name) for name in ("q", f"k{i}", f"v{i}")
+                                    for r in range(sp.world)])
+            kvs.append(kv)
+        return kvs
+
+    def close(self):
+        """Unmap the peer regions (collective over the Ulysses group)."""
+        if self.region is not None:
+            self.region.close()
 
     def inputs(self, seed: int):
         """This rank's shard of a chunk's synthetic inputs (identical global

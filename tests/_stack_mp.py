@@ -55,6 +55,7 @@ def main():
         print("block_rel", rb, "chunks_rel", rc, "sizes", sizes, flush=True)
         if rb <= 1e-2 and rc <= 1e-1:
             print("ULYSSES_OK", flush=True)
+    st.close()
     dist.barrier()
     dist.destroy_process_group()
 

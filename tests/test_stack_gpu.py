@@ -64,11 +64,16 @@ def test_kv_cache_ring(cuda):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ulysses_two_gpus_matches_one(cuda):
+@pytest.mark.parametrize("exchange,port", [("peer", 29517), ("nccl", 29518)])
+def test_ulysses_two_gpus_matches_one(cuda, exchange, port):
+    """P = 2 against P = 1 on the same seeded model: the exchange fused into the
+    QKV projection (peer stores over NVLink) and the NCCL all-to-all path."""
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([os.path.join(REPO, "joyai-video-edit_b200"),
-                                                        os.path.join(REPO, "tests")]))
+                                                        os.path.join(REPO, "tests")]),
+               JOYOMNI_SP_EXCHANGE=exchange, NCCL_NVLS_ENABLE="0")
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-                        "--master-addr=127.0.0.1", "--master-port=29517", os.path.join(REPO, "tests", "_stack_mp.py")],
+                        "--master-addr=127.0.0.1", f"--master-port={port}",
+                        os.path.join(REPO, "tests", "_stack_mp.py")],
                        capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "ULYSSES_OK" in r.stdout, r.stdout[-2000:]

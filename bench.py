@@ -384,9 +384,10 @@ def stack_bench(torch, dev, world):
            "fps": round(24 / (chunk_ms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
            "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
            "attention": "torch SDPA (cuDNN/flash), bf16",
-           "sp_exchange": ("none (P = 1)" if world == 1 else
-                           "q/k/v scattered by head in the QKV GEMM epilogue (peer stores over NVLink)"
-                           if st.region is not None else "NCCL all_to_all")}
+           "sp_exchange": ("NCCL all_to_all" if st.region is None else
+                           "q/k/v stored by head straight into the q buffer and K/V cache by the QKV GEMM "
+                           "epilogue" if world == 1 else
+                           "q/k/v scattered by head in the QKV GEMM epilogue (peer stores over NVLink)")}
     st.close()
     del st
     torch.cuda.empty_cache()

@@ -204,7 +204,7 @@ class Block:
         im = (self.img.mod + vec).unbind(0)
         tm = (self.txt.mod + vec).unbind(0)
 
-        if sp.world > 1 and kv.peer is not None:
+        if kv.peer is not None:
             return self._forward_peer(img, txt, im, tm, kv, sp)
 
         # ---- QKV of both streams into one [L_local, 3, H, Dh] buffer --------
@@ -235,10 +235,11 @@ class Block:
         return img, txt
 
     def _forward_peer(self, img, txt, im, tm, kv: "LayerKV", sp: SeqParallel):
-        """P > 1 with the exchange fused into the QKV projection: the epilogue
-        scatters q, k, v by head into the owning ranks' buffers (peer memory),
-        then every rank normalises / rotates its heads of all tokens, one
-        launch per rank segment of the gathered token order."""
+        """The QKV projection's epilogue scatters q, k, v by head into the owning
+        ranks' buffers (peer memory for P > 1; with P = 1 straight into this
+        rank's q buffer and K/V cache, which saves the two copies), then every
+        rank normalises / rotates its heads of all tokens, one launch per rank
+        segment of the gathered token order."""
         cfg = self.cfg
         Dh, D = cfg.head_dim, cfg.hidden
         Li = img.shape[0]
@@ -247,7 +248,8 @@ class Block:
         self.img.qkv.scatter(xq, xs, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0])
         tq, ts = norm_mod_quant(txt, tm[0], tm[1])
         self.txt.qkv.scatter(tq, ts, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0] + Li)
-        ex.region.sync()
+        if ex.region is not None:
+            ex.region.sync()
         q = ex.q
         for off, ni, nt, i0 in ex.seg:
             jo.qk_norm_rope_strided(q[off:off + ni][None], kv.k[off:off + ni][None], NORM_EPS, self.img.q_norm,
@@ -292,7 +294,7 @@ class Stack:
         self.region = None
         # P > 1: the QKV projections scatter into the owning ranks' buffers over
         # peer memory (JOYOMNI_SP_EXCHANGE=nccl selects the NCCL all-to-all path).
-        if self.sp.world > 1 and os.environ.get("JOYOMNI_SP_EXCHANGE", "peer") == "peer":
+        if os.environ.get("JOYOMNI_SP_EXCHANGE", "peer") == "peer":
             self.kv = self._peer_kv(n, cos, sin, device)
         else:
             self.kv = [LayerKV(cfg, self.sp, device) for _ in range(n)]
@@ -305,12 +307,12 @@ class Stack:
     def commit_kv(self):
         for kv in self.kv:
             kv.commit(self.sp)
-        if self.region is not None:
+        if self.region is not None and self.sp.world > 1:
             # the next chunk's scatters must not overtake a slower rank's commit copies
             self.region.sync()
 
     def _peer_kv(self, n: int, cos, sin, device) -> List["LayerKV"]:
-        from .peer import PeerRegion, RegionLayout
+        from .peer import LocalRegion, PeerRegion, RegionLayout
         cfg, sp = self.cfg, self.sp
         hpr, Dh = sp.local_heads, cfg.head_dim
         rows = sp.total_len + cfg.cache_chunks * cfg.img_tokens
@@ -319,7 +321,9 @@ class Stack:
         for i in range(n):
             lay.add(f"k{i}", (rows, hpr, Dh))
             lay.add(f"v{i}", (rows, hpr, Dh))
-        self.region = PeerRegion(lay, sp.group, sp.world, sp.rank, device)
+        # P = 1: the same layout in one local allocation, no peers to map
+        self.region = PeerRegion(lay, sp.group, sp.world, sp.rank, device) if sp.world > 1 else \
+            LocalRegion(lay, device)
         isz, tsz = split_sizes(cfg.img_tokens, sp.world), split_sizes(cfg.txt_tokens, sp.world)
         seg, off = [], 0
         for r in range(sp.world):
@@ -329,7 +333,7 @@ class Stack:
         kvs = []
         for i in range(n):
             kv = LayerKV(cfg, sp, device, k=self.region.tensor(f"k{i}"), v=self.region.tensor(f"v{i}"))
-            kv.peer = PeerExchange(self.region, q, seg, cos, sin,
+            kv.peer = PeerExchange(self.region if sp.world > 1 else None, q, seg, cos, sin,
                                    [self.region.ptr(r, name) for name in ("q", f"k{i}", f"v{i}")
                                     for r in range(sp.world)])
             kvs.append(kv)

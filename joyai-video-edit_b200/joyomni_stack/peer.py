@@ -45,6 +45,27 @@ class RegionLayout:
         return self.entries[name][0]
 
 
+class LocalRegion:
+    """The same layout in one local allocation (a single rank: nothing to map)."""
+
+    def __init__(self, layout: RegionLayout, device):
+        self.layout = layout
+        self.local = torch.empty(layout.size, dtype=torch.uint8, device=device)
+
+    def tensor(self, name: str) -> torch.Tensor:
+        return PeerRegion.tensor(self, name)
+
+    def ptr(self, rank: int, name: str) -> int:
+        assert rank == 0
+        return self.local.data_ptr() + self.layout.offset(name)
+
+    def sync(self) -> None:
+        pass
+
+    def close(self) -> None:
+        pass
+
+
 class PeerRegion:
     def __init__(self, layout: RegionLayout, group, world: int, rank: int, device):
         import torch.distributed as dist

@@ -264,7 +264,7 @@ constexpr int staged_max_threads(int vpl, int r) { return vpl * r >= 10 ? 256 : 
 // threads and kMaxTeams teams.
 constexpr int fixed_teams(int op, int norm, int vpl, int s, int r, int nw) {
   const int n = vpl * nw * 256;
-  const int tab = (op == OP_QUANT || is_modrow(op)) ? 0 : (norm == JO_NORM_LAYER ? 4 : 3) * n * 4;
+  const int tab = (op == OP_QUANT || is_modrow(op)) ? 0 : 2 * n * 4;
   const int per_team = s * r * n * 2 * (is_modrow(op) ? 3 : 1) + 2 * 4 * r * 16 * 4;
   int t = (224 * 1024 - tab) / per_team;
   if (t * nw * 32 > 1024) t = 1024 / (nw * 32);
@@ -298,12 +298,17 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
   // tensor-core sums already differ from a scalar loop in summation order).
   const float inv_n = 1.f / (float)N;
 
-  // ---- fp32 tables -------------------------------------------------------
-  constexpr int NTAB = (HAS_NORM && !MODROW) ? (NORM == JO_NORM_LAYER ? 4 : 3) : 0;
-  float* tg = reinterpret_cast<float*>(smem_raw);       // gamma
-  float* tsc = tg + N;                                  // 1 + scale
-  float* tsh = tsc + N;                                 // shift
-  float* tb = tsh + N;                                  // beta (layer norm only)
+  // ---- fp32 column tables (broadcast modulation) -------------------------
+  // The per-column constants are folded once per CTA:
+  //   rms:   y = (x * r) * A + B,             A = g * (1 + sc), B = sh
+  //   layer: y = ((x - mean) * r) * A + B,    A = g * (1 + sc), B = b * (1 + sc) + sh
+  // (1 + sc) is formed in fp32 as the reference does; the products and sums
+  // are regrouped, which moves an output by at most one bf16 ulp where the
+  // unrounded value sits at a rounding boundary (the row statistics already
+  // differ from the reference in summation order).
+  constexpr int NTAB = (HAS_NORM && !MODROW) ? 2 : 0;
+  float* tA = reinterpret_cast<float*>(smem_raw);
+  float* tB = tA + N;
   uint4* ring = reinterpret_cast<uint4*>(smem_raw + (size_t)NTAB * N * sizeof(float)) +
                 (size_t)tm * S * R * NST * nvec;
   // per-team reduction scratch [2 parities][4 slots][R * 16] after all rings
@@ -324,10 +329,10 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
     for (int i = tid; i < N; i += blockDim.x) {
       const int v = i >> 3, h = (i >> 2) & 1, e = i & 3;
       const int d = h * (N >> 1) + 4 * v + e;
-      tg[d] = has_g ? to_f32(g[i]) : 1.f;
-      if (NORM == JO_NORM_LAYER) tb[d] = has_b ? to_f32(b[i]) : 0.f;
-      tsc[d] = 1.f + to_f32(sc[i]);
-      tsh[d] = to_f32(sh[i]);
+      const float g1 = has_g ? to_f32(g[i]) : 1.f;
+      const float c1 = 1.f + to_f32(sc[i]);
+      tA[d] = __fmul_rn(g1, c1);
+      tB[d] = NORM == JO_NORM_LAYER ? __fmaf_rn(has_b ? to_f32(b[i]) : 0.f, c1, to_f32(sh[i])) : to_f32(sh[i]);
     }
     __syncthreads();
   }
@@ -509,15 +514,10 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c = h * (N >> 1) + 4 * (i * team + tl);
-          const float4 g = lds16f(tg + c);
-          const float4 sc = lds16f(tsc + c);
-          const float4 sh = lds16f(tsh + c);
-          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-          if constexpr (NORM == JO_NORM_LAYER) b = lds16f(tb + c);
-          const float2 g01 = make_float2(g.x, g.y), g23 = make_float2(g.z, g.w);
-          const float2 c01 = make_float2(sc.x, sc.y), c23 = make_float2(sc.z, sc.w);
-          const float2 s01 = make_float2(sh.x, sh.y), s23 = make_float2(sh.z, sh.w);
-          const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
+          const float4 A = lds16f(tA + c);
+          const float4 B = lds16f(tB + c);
+          const float2 a01 = make_float2(A.x, A.y), a23 = make_float2(A.z, A.w);
+          const float2 b01 = make_float2(B.x, B.y), b23 = make_float2(B.z, B.w);
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             uint32_t* wr = reinterpret_cast<uint32_t*>(&X[r][i].raw);
@@ -526,13 +526,13 @@ __global__ void __launch_bounds__(staged_threads(OP, NORM, VPL, S, R, NW), 1)
             float2 f1 = unpack2_r<T>(wr[2 * h + 1]);
             if constexpr (NORM == JO_NORM_LAYER) {
               const float2 nm = make_float2(-mean[r], -mean[r]);
-              f0 = fma2(fma2(mul2(add2(f0, nm), rv), g01, b01), c01, s01);
-              f1 = fma2(fma2(mul2(add2(f1, nm), rv), g23, b23), c23, s23);
+              f0 = fma2(mul2(add2(f0, nm), rv), a01, b01);
+              f1 = fma2(mul2(add2(f1, nm), rv), a23, b23);
             } else {
-              f0 = fma2(mul2(mul2(f0, rv), g01), c01, s01);
-              f1 = fma2(mul2(mul2(f1, rv), g23), c23, s23);
+              f0 = fma2(mul2(f0, rv), a01, b01);
+              f1 = fma2(mul2(f1, rv), a23, b23);
             }
-            wr[2 * h] = pack2<T>(f0.x, f0.y);      // RNE to T, as the reference's T(float) store
+            wr[2 * h] = pack2<T>(f0.x, f0.y);      // RNE to T
             wr[2 * h + 1] = pack2<T>(f1.x, f1.y);
             if constexpr (QOUT) {
               acc[r] = absmax_h2<T>(acc[r], wr[2 * h]);
@@ -567,8 +567,7 @@ int launch(const Args& a, int team, cudaStream_t st) {
   const int nvec = a.N / 8;
   if (NW > 0 && (team != NW * 32 || nvec != VPL * NW * 32)) return JO_ERR_INVALID;
   constexpr int NST = is_modrow(OP) ? 3 : 1;
-  const size_t tab = (OP != OP_QUANT && !is_modrow(OP))
-                         ? (size_t)(NORM == JO_NORM_LAYER ? 4 : 3) * a.N * sizeof(float) : 0;
+  const size_t tab = (OP != OP_QUANT && !is_modrow(OP)) ? (size_t)2 * a.N * sizeof(float) : 0;
   const size_t per_team = (size_t)S * R * NST * nvec * 16 + (size_t)2 * 4 * R * 16 * sizeof(float);
   // Up to 640 threads and ~224 KB of shared memory per CTA, one CTA per SM.
   int teams = NW > 0 ? fixed_teams(OP, NORM, VPL, S, R, NW) : staged_max_threads(VPL, R) / team;

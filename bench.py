@@ -312,7 +312,7 @@ def run_ours(args):
             "gpu_launches": K,  # timed region of `value`; the e2e region adds K * E2E_CHUNKS chunk launches
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": args.traffic,
-                         "peak_source": pk["source"], "kernel": "staged_rows<bf16,NORM_MOD_QUANT,RMS,vpl5,S2,R2,4 warps>",
+                         "peak_source": pk["source"], "kernel": "staged_rows<bf16,NORM_MOD_QUANT,RMS,vpl10,S2,R1,2-warp teams>",
                          "avg_launch_us": round(avg_launch_us, 3)},
             "clocks": clocks,
         }

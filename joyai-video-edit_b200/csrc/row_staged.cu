@@ -596,7 +596,7 @@ struct StagedGeom {
   int vpl, r, s;
 };
 
-static StagedGeom pick_geom(int nvec) {
+static StagedGeom pick_geom(int nvec, int op, int norm) {
   // JO_STAGED_GEOM="vpl,r,s" overrides the choice (used to compare geometries).
   static int ov = -1;
   static StagedGeom g_ov{4, 2, 2};
@@ -611,9 +611,18 @@ static StagedGeom pick_geom(int nvec) {
     }
   }
   if (ov == 1) return g_ov;
-  // N = 5120: 4-warp teams of 5 vectors per thread, two rows per iteration
-  // (fixed-geometry instantiation; measured best of the fixed set).
-  if (nvec == 640) return StagedGeom{5, 2, 2};
+  // N = 5120: fixed-geometry instantiations, the measured best (B200,
+  // M = 10530).  The broadcast norm -> modulate and its fused quantising form
+  // share one geometry per norm type, so their row statistics are summed in
+  // the same order and the fused codes equal quantising the bf16 output:
+  // rms 2-warp teams of 10 vectors per thread, layer 4-warp teams of 5 (also
+  // quantisation alone); per-row modulation 4-warp teams of 5, two rows.
+  if (nvec == 640) {
+    if ((op == staged::OP_NORM_MOD_QUANT || op == staged::OP_NORM_MOD) && norm == JO_NORM_RMS)
+      return StagedGeom{10, 1, 2};
+    if (staged::is_modrow(op)) return StagedGeom{5, 2, 2};
+    return StagedGeom{5, 1, 2};
+  }
   return StagedGeom{4, 2, 2};
 }
 
@@ -647,7 +656,6 @@ static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream
   if (fixed_enabled() && N_FIXED_OK(g, nvec)) {
 #define JO_F(V, R, S, W) \
   if (g.vpl == V && g.r == R && g.s == S && nvec == V * W * 32) return launch<T, OP, NORM, V, S, R, W>(a, team, st);
-    JO_F(4, 1, 2, 5)
     JO_F(5, 1, 2, 4)
     JO_F(5, 2, 2, 4)
     JO_F(10, 1, 2, 2)
@@ -675,7 +683,7 @@ int staged_rows_launch(int op, int norm, int dtype, const void* x, void* y, cons
   if (N % 8 != 0 || nvec < 128) return JO_ERR_INVALID;
   if (is_modrow(op) && (mod_group < 1 || mod_stride < N)) return JO_ERR_INVALID;
   Args a{x, y, gamma, beta, scale, shift, q, s, mod_stride, mod_group, M, N, eps};
-  const StagedGeom g = pick_geom(nvec);
+  const StagedGeom g = pick_geom(nvec, op, norm);
 #define JO_ST(T)                                                                                          \
   do {                                                                                                    \
     if (op == OP_QUANT) return launch_geom<T, OP_QUANT, JO_NORM_RMS>(a, nvec, g, st);                    \

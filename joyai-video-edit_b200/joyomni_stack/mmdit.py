@@ -294,9 +294,10 @@ class Stack:
         self.region = None
         # P > 1: the QKV projections scatter into the owning ranks' buffers over
         # peer memory (JOYOMNI_SP_EXCHANGE=nccl selects the NCCL all-to-all path).
+        self.kv = None
         if os.environ.get("JOYOMNI_SP_EXCHANGE", "peer") == "peer":
-            self.kv = self._peer_kv(n, cos, sin, device)
-        else:
+            self.kv = self._peer_kv_agreed(n, cos, sin, device)
+        if self.kv is None:
             self.kv = [LayerKV(cfg, self.sp, device) for _ in range(n)]
 
     def forward(self, img, txt, vec):
@@ -310,6 +311,31 @@ class Stack:
         if self.region is not None and self.sp.world > 1:
             # the next chunk's scatters must not overtake a slower rank's commit copies
             self.region.sync()
+
+    def _peer_kv_agreed(self, n: int, cos, sin, device) -> Optional[List["LayerKV"]]:
+        """The peer exchange when every rank could set it up (IPC export / map),
+        else None on every rank (the NCCL path): the ranks agree on the outcome
+        with a MIN all-reduce, so no rank scatters into a rank that cannot."""
+        try:
+            kvs, err = self._peer_kv(n, cos, sin, device), None
+        except Exception as e:  # noqa: BLE001
+            kvs, err = None, e
+        if self.sp.world > 1:
+            import torch.distributed as dist
+            ok = torch.tensor([1.0 if kvs is not None else 0.0], device=device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.sp.group)
+            if ok.item() < 1.0:
+                self.exchange_error = repr(err)[:300] if err is not None else "a peer rank failed"
+                if torch.cuda.is_available():
+                    torch.cuda.synchronize()
+                dist.barrier(group=self.sp.group)      # every rank, including the failed one
+                if self.region is not None:
+                    self.region.close(barrier=False)
+                self.region = None
+                return None
+        elif kvs is None:
+            raise err
+        return kvs
 
     def _peer_kv(self, n: int, cos, sin, device) -> List["LayerKV"]:
         from .peer import LocalRegion, PeerRegion, RegionLayout

@@ -112,13 +112,13 @@ class PeerRegion:
         import torch.distributed as dist
         dist.all_reduce(self._flag, group=self.group)
 
-    def close(self) -> None:
-        """Unmap the peers' regions (after a barrier, so no rank still writes)."""
+    def close(self, barrier: bool = True) -> None:
+        """Unmap the peers' regions, after a barrier so that no rank still
+        writes (barrier=False: the caller has synchronised every rank)."""
         import torch.distributed as dist
-        if not self._opened:
-            return
-        torch.cuda.synchronize()
-        dist.barrier(group=self.group)
+        if barrier:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
         for p in self._opened:
             _lib.check(_lib.lib.jo_ipc_close(p))
         self._opened = []

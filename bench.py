@@ -10,10 +10,14 @@ GB/s (x read once + codes + scales written once + the three [N] vectors).
   value : device throughput, inputs resident in HBM; K steps replayed from a CUDA
           graph over 3 rotating input/output sets (485 MB > 126 MB L2).
   e2e   : the same step through the public Python API with pinned host buffers:
-          H2D of x and D2H of codes+scales inside the timed region.
+          H2D of x and D2H of codes+scales inside the timed region, the rows
+          streamed in 8 chunks on 3 CUDA streams (upload / kernel / download
+          overlap).
 Extra keys: per-kernel lines for the other configs ("kernels"), the reference's
 own CUDA kernels timed on the same box ("reference_gpu", when oracle/_ref is
-present), the CPU oracle baseline ("cpu_baseline"), the roofline, SM clocks.
+present), the CPU oracle baseline ("cpu_baseline"), the roofline, SM clocks,
+and the block stack of configs 4/5 ("stack": Ulysses over all ranks, with the
+q/k/v exchange fused into the QKV GEMM epilogue).
 
 Multi-GPU (torchrun): every rank runs the same per-rank workload on its own
 rows (the ops are independent per token; no collective on the data path),

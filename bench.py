@@ -547,13 +547,18 @@ def cpu_baseline(seconds):
     rows = int(max(256, min(M_CFG2, rows * seconds / max(dt, 1e-3))))
     x, w, sh, sc = _cpu_sample(rows)
     _cpu_step(x, w, sh, sc, threads)
-    t0 = time.perf_counter()
-    _cpu_step(x, w, sh, sc, threads)
-    dt = time.perf_counter() - t0
-    gbs = cfg2_bytes(rows, N_CFG2) / dt / 1e9
+    # repeat whole passes over the sample until about `seconds` of CPU work
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        _cpu_step(x, w, sh, sc, threads)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if (dt >= seconds and reps >= 3) or reps >= 10000:
+            break
+    gbs = cfg2_bytes(rows, N_CFG2) * reps / dt / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {M_CFG2} rows of cfg2, eager-torch fp32 restatement of the reference "
-                      f"(norm_scale_shift RMS then per-token quant), {threads} threads, {dt:.2f} s"}
+            "sample": f"{reps} passes over {rows} of {M_CFG2} rows of cfg2, eager-torch fp32 restatement of the "
+                      f"reference (norm_scale_shift RMS then per-token quant), {threads} threads, {dt:.1f} s"}
 
 
 def run_reference(args):

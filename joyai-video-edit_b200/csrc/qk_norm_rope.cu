@@ -134,19 +134,26 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 
 // One (token, head) slot's q or k vector of this lane: RMS over the head in
 // the reference's summation order, weight, then the interleaved-pair rotation.
-// wf: this lane's 8 weights (fp32); cf / sf: this lane's 4 cos / sin entries
-// (fp32, shared by the q and the k vector of the slot).
-template <int D, bool ROPE>
-__device__ __forceinline__ uint4 norm_rope_vec(uint4 raw, const float (&wf)[8], const float (&cf)[4],
-                                               const float (&sf)[4], float eps) {
-  constexpr int LPH = D / 8;
-  constexpr int P = 256 / D;
-  constexpr int EP = 8 / P;
-  Vec16<__nv_bfloat16> v;
-  v.raw = raw;
-  float e[8];
+// The lane holds EL consecutive elements of the head (EL / 8 16-byte words),
+// i.e. the partials of P = EL / (D / 32) consecutive lanes of the reference's
+// 32-lane reduction; they are kept separate through the butterfly over the
+// lane bits held by other lanes and combined locally in the order of the
+// remaining bits, which reproduces the reference sum bit for bit (every lane
+// of an xor butterfly ends with the same bits).  wf: this lane's EL weights;
+// cf / sf: its EL / 2 cos / sin entries (shared by q and k of the slot).
+template <int D, int EL, bool ROPE>
+__device__ __forceinline__ void norm_rope_lane(uint4 (&v)[EL / 8], const float (&wf)[EL], const float (&cf)[EL / 2],
+                                               const float (&sf)[EL / 2], float eps) {
+  constexpr int LPH = D / EL;
+  constexpr int EP = D / 32;
+  constexpr int P = EL / EP;
+  float e[EL];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) e[j] = v.get(j);
+  for (int j = 0; j < EL; j += 2) {
+    const float2 f = unpack2<__nv_bfloat16>((&v[j / 8].x)[(j % 8) / 2]);
+    e[j] = f.x;
+    e[j + 1] = f.y;
+  }
   float part[P];
 #pragma unroll
   for (int p = 0; p < P; ++p) {
@@ -165,29 +172,18 @@ __device__ __forceinline__ uint4 norm_rope_vec(uint4 raw, const float (&wf)[8], 
     for (int p = 0; p < m; ++p) part[p] = part[p] + part[p + m];
   const float rms_rcp = rsqrtf(part[0] / static_cast<float>(D) + eps);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) e[j] *= rms_rcp * wf[j];
-  if (!ROPE) {
+  for (int j = 0; j < EL; ++j) e[j] *= rms_rcp * wf[j];
 #pragma unroll
-    for (int j = 0; j < 8; j += 2)
-      reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(e[j], e[j + 1]));
-    return v.raw;
+  for (int j = 0; j < EL; j += 2) {
+    float o0 = e[j], o1 = e[j + 1];
+    if (ROPE) {
+      const float c = cf[j / 2], s = sf[j / 2];
+      const float x1 = e[j], x2 = e[j + 1];
+      o0 = x1 * c - x2 * s;
+      o1 = x1 * s + x2 * c;
+    }
+    (&v[j / 8].x)[(j % 8) / 2] = pack2<__nv_bfloat16>(o0, o1);
   }
-#pragma unroll
-  for (int j = 0; j < 8; j += 2) {
-    const float c = cf[j / 2];
-    const float s = sf[j / 2];
-    const float x1 = e[j], x2 = e[j + 1];
-    const float o0 = x1 * c - x2 * s;
-    const float o1 = x1 * s + x2 * c;
-    reinterpret_cast<__nv_bfloat162*>(&v.raw)[j / 2] = __float22bfloat162_rn(make_float2(o0, o1));
-  }
-  return v.raw;
-}
-__device__ __forceinline__ void unpack_cs(uint2 c2, uint2 s2, float (&cf)[4], float (&sf)[4]) {
-  const float2 c01 = unpack2<__nv_bfloat16>(c2.x), c23 = unpack2<__nv_bfloat16>(c2.y);
-  const float2 s01 = unpack2<__nv_bfloat16>(s2.x), s23 = unpack2<__nv_bfloat16>(s2.y);
-  cf[0] = c01.x; cf[1] = c01.y; cf[2] = c23.x; cf[3] = c23.y;
-  sf[0] = s01.x; sf[1] = s01.y; sf[2] = s23.x; sf[3] = s23.y;
 }
 
 __device__ __forceinline__ void cpa16(void* smem, const void* g) {
@@ -208,25 +204,35 @@ __device__ __forceinline__ void cpa_wait() {
 // warp owns a contiguous run of slot groups (HPW slots each, so mostly heads
 // of one token), balanced to within one group, which it walks with a cursor
 // (token, head, position in the RoPE table) advanced by HPW heads per group --
-// no division per group.  The groups ahead are staged by each thread into its
-// own shared-memory slots with cp.async (S - 1 groups in flight per thread at
-// no register cost); a thread only reads back the slots it filled itself,
-// after cp.async.wait_group, so no barrier is needed.  Slot layout
-// [stage][q | k | cos,sin][thread]: consecutive threads touch consecutive
-// 16-byte words (conflict-free).  Every lane of a warp runs the same number of
-// iterations (the head reduction shuffles need the full warp); slots past the
-// end are masked.
-template <int D, int S, bool ROPE>
+// no division per group.  Each lane moves EL elements of a head.  The groups
+// ahead are staged by each thread into its own shared-memory slots with
+// cp.async (S - 1 groups in flight per thread at no register cost); a thread
+// only reads back the slots it filled itself, after cp.async.wait_group, so no
+// barrier is needed.  Slot layout [stage][word][thread] (dynamic shared
+// memory): consecutive threads touch consecutive 16-byte words
+// (conflict-free).  Every lane of a warp runs the same number of iterations
+// (the head reduction shuffles need the full warp); slots past the end are
+// masked.
+template <int EL>
+struct RingWords {
+  static constexpr int V = EL / 8;            // 16-byte words of q (and of k)
+  static constexpr int CS = EL == 8 ? 1 : 2;  // words of cos + sin
+  static constexpr int N = 2 * V + CS;
+};
+
+template <int D, int EL, int S, bool ROPE>
 __global__ void __launch_bounds__(256) qk_norm_rope_ring(
     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, int64_t slots, int seq_len, int num_heads,
     float eps, const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
     const __nv_bfloat16* __restrict__ cosp, const __nv_bfloat16* __restrict__ sinp, int64_t q_ts, int64_t k_ts) {
-  constexpr int LPH = D / 8;
+  constexpr int LPH = D / EL;
   constexpr int HPW = 32 / LPH;
-  __shared__ uint4 ring[S][3][256];
+  constexpr int V = RingWords<EL>::V;
+  constexpr int NW = RingWords<EL>::N;
+  extern __shared__ uint4 ring_raw[];
+  auto slotw = [&](int stage, int w) -> uint4* { return ring_raw + ((size_t)stage * NW + w) * 256 + threadIdx.x; };
   const int lane = threadIdx.x & 31;
   const int hl = lane % LPH;
-  const int t = threadIdx.x;
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
 
@@ -237,15 +243,16 @@ __global__ void __launch_bounds__(256) qk_norm_rope_ring(
   const int ng = (int)(base + (warp < rem ? 1 : 0));
   if (ng == 0) return;  // warp-uniform
 
-  float wqf[8], wkf[8];
-  {
+  float wqf[EL], wkf[EL];
+#pragma unroll
+  for (int w = 0; w < V; ++w) {
     Vec16<__nv_bfloat16> a, b;
-    a.raw = ld_cached(qw + hl * 8);
-    b.raw = ld_cached(kw + hl * 8);
+    a.raw = ld_cached(qw + hl * EL + w * 8);
+    b.raw = ld_cached(kw + hl * EL + w * 8);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      wqf[j] = a.get(j);
-      wkf[j] = b.get(j);
+      wqf[w * 8 + j] = a.get(j);
+      wkf[w * 8 + j] = b.get(j);
     }
   }
 
@@ -269,12 +276,24 @@ __global__ void __launch_bounds__(256) qk_norm_rope_ring(
   };
   auto issue = [&](int stage) {
     if (ci.slot < (uint64_t)slots) {
-      cpa16(&ring[stage][0][t], q + ((int64_t)ci.tok * q_ts + ci.head * D + hl * 8));
-      cpa16(&ring[stage][1][t], k + ((int64_t)ci.tok * k_ts + ci.head * D + hl * 8));
+      const __nv_bfloat16* qs = q + ((int64_t)ci.tok * q_ts + ci.head * D + hl * EL);
+      const __nv_bfloat16* ks = k + ((int64_t)ci.tok * k_ts + ci.head * D + hl * EL);
+#pragma unroll
+      for (int w = 0; w < V; ++w) {
+        cpa16(slotw(stage, w), qs + w * 8);
+        cpa16(slotw(stage, V + w), ks + w * 8);
+      }
       if (ROPE) {
-        uint2* cs = reinterpret_cast<uint2*>(&ring[stage][2][t]);
-        cpa8(cs, cosp + (int64_t)ci.tr * (D / 2) + hl * 4);
-        cpa8(cs + 1, sinp + (int64_t)ci.tr * (D / 2) + hl * 4);
+        const __nv_bfloat16* cs = cosp + (int64_t)ci.tr * (D / 2) + hl * (EL / 2);
+        const __nv_bfloat16* ss = sinp + (int64_t)ci.tr * (D / 2) + hl * (EL / 2);
+        if constexpr (EL == 8) {
+          uint2* d = reinterpret_cast<uint2*>(slotw(stage, 2 * V));
+          cpa8(d, cs);
+          cpa8(d + 1, ss);
+        } else {
+          cpa16(slotw(stage, 2 * V), cs);
+          cpa16(slotw(stage, 2 * V + 1), ss);
+        }
       }
     }
     cpa_commit();
@@ -293,51 +312,78 @@ __global__ void __launch_bounds__(256) qk_norm_rope_ring(
     si = si + 1 == S ? 0 : si + 1;
     cpa_wait<S - 1>();
     const bool ok = cc.slot < (uint64_t)slots;
-    uint4 vq = make_uint4(0, 0, 0, 0), vk = vq;
-    uint2 c2 = make_uint2(0, 0), s2 = c2;
-    if (ok) {
-      vq = ring[sc][0][t];
-      vk = ring[sc][1][t];
-      if (ROPE) {
-        const uint4 cs = ring[sc][2][t];
-        c2 = make_uint2(cs.x, cs.y);
-        s2 = make_uint2(cs.z, cs.w);
+    uint4 vq[V], vk[V];
+    float cf[EL / 2], sf[EL / 2];
+#pragma unroll
+    for (int w = 0; w < V; ++w) {
+      vq[w] = ok ? *slotw(sc, w) : make_uint4(0, 0, 0, 0);
+      vk[w] = ok ? *slotw(sc, V + w) : make_uint4(0, 0, 0, 0);
+    }
+    if (ROPE) {
+      uint32_t cw[EL / 4], sw[EL / 4];
+      if constexpr (EL == 8) {
+        const uint4 cs = ok ? *slotw(sc, 2 * V) : make_uint4(0, 0, 0, 0);
+        cw[0] = cs.x; cw[1] = cs.y; sw[0] = cs.z; sw[1] = cs.w;
+      } else {
+        const uint4 c4 = ok ? *slotw(sc, 2 * V) : make_uint4(0, 0, 0, 0);
+        const uint4 s4 = ok ? *slotw(sc, 2 * V + 1) : make_uint4(0, 0, 0, 0);
+        cw[0] = c4.x; cw[1] = c4.y; cw[2] = c4.z; cw[3] = c4.w;
+        sw[0] = s4.x; sw[1] = s4.y; sw[2] = s4.z; sw[3] = s4.w;
       }
+#pragma unroll
+      for (int j = 0; j < EL / 4; ++j) {
+        const float2 c = unpack2<__nv_bfloat16>(cw[j]), sn = unpack2<__nv_bfloat16>(sw[j]);
+        cf[2 * j] = c.x; cf[2 * j + 1] = c.y;
+        sf[2 * j] = sn.x; sf[2 * j + 1] = sn.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EL / 2; ++j) cf[j] = sf[j] = 0.f;
     }
     sc = sc + 1 == S ? 0 : sc + 1;
-    float cf[4], sf[4];
-    unpack_cs(c2, s2, cf, sf);
-    const uint4 oq = norm_rope_vec<D, ROPE>(vq, wqf, cf, sf, eps);
-    const uint4 okv = norm_rope_vec<D, ROPE>(vk, wkf, cf, sf, eps);
+    norm_rope_lane<D, EL, ROPE>(vq, wqf, cf, sf, eps);
+    norm_rope_lane<D, EL, ROPE>(vk, wkf, cf, sf, eps);
     if (ok) {
-      st_stream(q + ((int64_t)cc.tok * q_ts + cc.head * D + hl * 8), oq);
-      st_stream(k + ((int64_t)cc.tok * k_ts + cc.head * D + hl * 8), okv);
+      __nv_bfloat16* qd = q + ((int64_t)cc.tok * q_ts + cc.head * D + hl * EL);
+      __nv_bfloat16* kd = k + ((int64_t)cc.tok * k_ts + cc.head * D + hl * EL);
+#pragma unroll
+      for (int w = 0; w < V; ++w) {
+        st_stream(qd + w * 8, vq[w]);
+        st_stream(kd + w * 8, vk[w]);
+      }
     }
     advance(cc);
   }
   cpa_wait<0>();
 }
 
-template <int D, int S>
+template <int D, int EL, int S>
 int launch_ring(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw,
                 const void* kw, const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
-  constexpr int HPW = 32 / (D / 8);
+  constexpr int HPW = 32 / (D / EL);
   auto* qp = static_cast<__nv_bfloat16*>(q);
   auto* kp = static_cast<__nv_bfloat16*>(k);
   auto* qwp = static_cast<const __nv_bfloat16*>(qw);
   auto* kwp = static_cast<const __nv_bfloat16*>(kw);
   auto* cp = static_cast<const __nv_bfloat16*>(c);
   auto* sp = static_cast<const __nv_bfloat16*>(s);
-  auto kern = c ? qk_norm_rope_ring<D, S, true> : qk_norm_rope_ring<D, S, false>;
+  auto kern = c ? qk_norm_rope_ring<D, EL, S, true> : qk_norm_rope_ring<D, EL, S, false>;
+  const int smem = S * RingWords<EL>::N * 256 * 16;
   static int per_sm[2] = {0, 0};
   int& bps = per_sm[c ? 1 : 0];
-  if (bps == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kern, 256, 0) != cudaSuccess || bps < 1))
-    bps = 1;
+  if (bps == 0) {
+    cudaFuncSetAttribute(qk_norm_rope_ring<D, EL, S, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(qk_norm_rope_ring<D, EL, S, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kern, 256, smem) != cudaSuccess || bps < 1) {
+      cudaGetLastError();
+      bps = 1;
+    }
+  }
   const int64_t groups = (slots + HPW - 1) / HPW;
   const int64_t need = (groups + 7) / 8;  // one group per warp at least
   const int64_t wave = (int64_t)bps * sm_count();
   const int64_t blocks = need < wave ? need : wave;
-  kern<<<(unsigned)blocks, 256, 0, st>>>(qp, kp, slots, seq_len, num_heads, eps, qwp, kwp, cp, sp, q_ts, k_ts);
+  kern<<<(unsigned)blocks, 256, smem, st>>>(qp, kp, slots, seq_len, num_heads, eps, qwp, kwp, cp, sp, q_ts, k_ts);
   return check_launch("fused_qk_norm_rope_3d_paired");
 }
 
@@ -364,7 +410,7 @@ int launch_u(void* q, void* k, int64_t slots, int seq_len, int num_heads, float 
 
 // Kernel choice for measurements: JO_QKR_U=1/2 selects the one-shot kernel
 // (one slot group per warp, U groups), JO_QKR_S=2/4 the ring depth of the
-// persistent ring kernel (default, 3 stages).
+// persistent ring kernel (default, 3 stages), JO_QKR_EL=8 its 8-element lanes.
 static int env_int(const char* name, int dflt) {
   const char* e = getenv(name);
   return e ? atoi(e) : dflt;
@@ -373,12 +419,22 @@ static int env_int(const char* name, int dflt) {
 template <int D>
 int launch(void* q, void* k, int64_t slots, int seq_len, int num_heads, float eps, const void* qw, const void* kw,
            const void* c, const void* s, int64_t q_ts, int64_t k_ts, cudaStream_t st) {
-  static const int u = env_int("JO_QKR_U", 0), ring = env_int("JO_QKR_S", 3);
+  // 8 elements per lane (D / 8 lanes per head) by default; JO_QKR_EL=16 gives
+  // each lane 16 (fewer shuffles and per-slot overhead per element, but 104
+  // registers: measured 26.7 against 16.2 us on config 1).
+  static const int u = env_int("JO_QKR_U", 0), ring = env_int("JO_QKR_S", 3), el = env_int("JO_QKR_EL", 8);
   if (u == 1) return launch_u<D, 1>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
   if (u == 2) return launch_u<D, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-  if (ring == 2) return launch_ring<D, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-  if (ring == 4) return launch_ring<D, 4>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
-  return launch_ring<D, 3>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  // 16-element lanes stage cos / sin rows with 16-byte copies: tables that are
+  // only 8-byte aligned take the 8-element form.
+  if (el != 16 || (c && !(aligned16(c) && aligned16(s)))) {
+    if (ring == 2) return launch_ring<D, 8, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+    if (ring == 4) return launch_ring<D, 8, 4>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+    return launch_ring<D, 8, 3>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  }
+  if (ring == 2) return launch_ring<D, 16, 2>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  if (ring == 4) return launch_ring<D, 16, 4>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
+  return launch_ring<D, 16, 3>(q, k, slots, seq_len, num_heads, eps, qw, kw, c, s, q_ts, k_ts, st);
 }
 
 }  // namespace

@@ -164,14 +164,16 @@ int jo_gemm_last_fault(int reset);
  * tok0 + m, local head h % heads_per_rank of a [tokens, heads_per_rank,
  * head_dim] buffer: the all-to-all that turns a token shard into a head shard
  * (replaces torch.distributed.all_to_all_single after the QKV projection).
- * Destinations of other ranks are peer pointers from jo_ipc_open.  The caller
+ * Every destination holds dst_tokens token rows and tok0 + M <= dst_tokens
+ * is required (JO_ERR_INVALID otherwise): a destination may be another GPU's
+ * memory.  Destinations of other ranks are peer pointers from jo_ipc_open.  The caller
  * synchronises the ranks (e.g. a one-element collective on the same stream)
  * before any rank reads its buffers.
  */
 int jo_fp8_scaled_mm_scatter(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
                              const void* bias, int64_t M, int64_t N, int64_t K, int out_dtype,
                              const void* const* dst, int parts, int ranks, int heads_per_rank, int head_dim,
-                             int64_t tok0, void* stream);
+                             int64_t tok0, int64_t dst_tokens, void* stream);
 
 /*
  * Peer-memory plumbing (legacy CUDA IPC, no multicast objects) for the

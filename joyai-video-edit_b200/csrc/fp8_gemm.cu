@@ -46,6 +46,10 @@ constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
+// Sticky fault code of the bounded mbarrier waits, one per device and shared
+// by every GEMM launch on it: the first wait that times out records its code
+// (the output of that launch is then incomplete).  Read and cleared by
+// jo_gemm_last_fault(); the stack harness checks it once per chunk.
 __device__ int g_fault = 0;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -701,9 +705,12 @@ static bool use_2sm() {
 template <typename OutT>
 int launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, Params p, cudaStream_t st) {
   const int smem = STAGES2 * STAGE2_BYTES + 1024 + 256;
-  static bool attr = false;
-  static int max_pairs = 0;
-  if (!attr) {
+  // The shared-memory opt-in and the occupancy query are per device: a
+  // process may launch on several GPUs.
+  const int dev = device_slot();
+  static bool attr[kMaxDevices] = {};
+  static int max_pairs_dev[kMaxDevices] = {};
+  if (!attr[dev]) {
     cudaFuncSetAttribute(fp8_gemm_2sm_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaLaunchConfig_t q = {};
     q.gridDim = dim3(2 * 74);
@@ -721,9 +728,10 @@ int launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, Params p, cudaStrea
       cudaGetLastError();
       nc = sm_count() / 2;
     }
-    max_pairs = nc;
-    attr = true;
+    max_pairs_dev[dev] = nc;
+    attr[dev] = true;
   }
+  const int max_pairs = max_pairs_dev[dev];
   p.m_blocks = (p.M + 255) / 256;
   static int group_env = -1;
   if (group_env < 0) {
@@ -785,10 +793,11 @@ int launch(const void* A, const void* B, const float* sa, const float* sb, const
   for (int i = 0; i < 24; ++i) p.sc_dst[i] = sc ? sc->dst[i] : nullptr;
   if (pair) return launch_2sm<OutT>(ta, tb, p, st);
   const int smem = STAGES * STAGE_BYTES + 1024 + 256;
-  static bool attr = false;
-  if (!attr) {
+  const int dev = device_slot();
+  static bool attr[kMaxDevices] = {};
+  if (!attr[dev]) {
     cudaFuncSetAttribute(fp8_gemm_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
+    attr[dev] = true;
   }
   const int tiles = p.m_blocks * p.n_blocks;
   const int grid = tiles < sm_count() ? tiles : sm_count();
@@ -848,14 +857,14 @@ int jo_fp8_scaled_mm(const void* mat_a, const void* mat_b, const float* scales_a
 // heads_per_rank*head_dim] result to the rank that owns the head (the
 // sequence-parallel all-to-all fused into the GEMM).  dst[part * ranks + r] is
 // rank r's [tokens, heads_per_rank, head_dim] buffer for part `part` (a peer
-// pointer for r != this rank, opened with jo_ipc_open); row m lands at token
-// tok0 + m.  Stores only (no TMA, no multicast); each epilogue thread ends
+// pointer for r != this rank, opened with jo_ipc_open) of dst_tokens token
+// rows; row m lands at token tok0 + m < dst_tokens.  Stores only (no TMA, no multicast); each epilogue thread ends
 // with a system-scope fence, and the caller orders the consumers after a
 // cross-rank synchronisation.
 int jo_fp8_scaled_mm_scatter(const void* mat_a, const void* mat_b, const float* scales_a, const float* scales_b,
                              const void* bias, int64_t M, int64_t N, int64_t K, int out_dtype,
                              const void* const* dst, int parts, int ranks, int heads_per_rank, int head_dim,
-                             int64_t tok0, void* stream) {
+                             int64_t tok0, int64_t dst_tokens, void* stream) {
   using namespace jo;
   const char* what = "fp8_scaled_mm_scatter";
   JO_REQUIRE(out_dtype == JO_DTYPE_BF16 || out_dtype == JO_DTYPE_F16, JO_ERR_DTYPE,
@@ -868,6 +877,11 @@ int jo_fp8_scaled_mm_scatter(const void* mat_a, const void* mat_b, const float* 
   JO_REQUIRE(M >= 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && K % 16 == 0,
              JO_ERR_INVALID, "%s: invalid shape", what);
   JO_REQUIRE(M == 0 || (mat_a && mat_b && scales_a && scales_b && dst), JO_ERR_INVALID, "%s: null pointer", what);
+  // Every destination holds dst_tokens token rows; rows tok0 .. tok0+M-1 must
+  // fit, since a destination may be another GPU's memory.
+  JO_REQUIRE(dst_tokens >= 0 && tok0 + M <= dst_tokens, JO_ERR_INVALID,
+             "%s: rows %lld..%lld do not fit destinations of %lld tokens", what, (long long)tok0,
+             (long long)(tok0 + M), (long long)dst_tokens);
   JO_REQUIRE(aligned16(mat_a) && aligned16(mat_b) && aligned16(scales_b) && (!bias || aligned8(bias)),
              JO_ERR_ALIGN, "%s: operands must be 16-byte aligned (bias 8-byte)", what);
   gemm::ScatterSpec sc;

@@ -41,6 +41,19 @@ int check_launch(const char* what);
 // Number of SMs of the current device (cached).
 int sm_count();
 
+// Launch-configuration caches (shared-memory opt-ins, occupancy) are kept per
+// device, since a process may launch on several GPUs.
+constexpr int kMaxDevices = 64;
+// Index of the current device, clamped into [0, kMaxDevices).
+inline int device_slot() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    cudaGetLastError();
+    d = 0;
+  }
+  return d < 0 ? 0 : d % kMaxDevices;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 
@@ -189,7 +202,12 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 
 // a / 448 correctly rounded, for a = |x| of a 16-bit (bf16 or fp16) value:
-// one multiply by RN(1/448) and one FMA correction step.  Checked exhaustively
+// one multiply by RN(1/448) and one FMA correction step -- Markstein's
+// residual correction (P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with
+// q = RN(a*c), the residual r = a - q*448 is exact in one FMA, and
+// RN(q + r*c) is the correctly rounded quotient when c = RN(1/448) and the
+// dividend range is limited as here.  Checked exhaustively
 // against the exact quotient for every finite positive bf16 and fp16 value
 // (tests/test_oracle.py emulates the three roundings with exact rationals).
 __device__ __forceinline__ float div448_h(float a) {

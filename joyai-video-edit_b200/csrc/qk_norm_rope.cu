@@ -369,8 +369,8 @@ int launch_ring(void* q, void* k, int64_t slots, int seq_len, int num_heads, flo
   auto* sp = static_cast<const __nv_bfloat16*>(s);
   auto kern = c ? qk_norm_rope_ring<D, EL, S, true> : qk_norm_rope_ring<D, EL, S, false>;
   const int smem = S * RingWords<EL>::N * 256 * 16;
-  static int per_sm[2] = {0, 0};
-  int& bps = per_sm[c ? 1 : 0];
+  static int per_sm[kMaxDevices][2] = {};
+  int& bps = per_sm[device_slot()][c ? 1 : 0];
   if (bps == 0) {
     cudaFuncSetAttribute(qk_norm_rope_ring<D, EL, S, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(qk_norm_rope_ring<D, EL, S, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -410,7 +410,8 @@ int launch_u(void* q, void* k, int64_t slots, int seq_len, int num_heads, float 
 
 // Kernel choice for measurements: JO_QKR_U=1/2 selects the one-shot kernel
 // (one slot group per warp, U groups), JO_QKR_S=2/4 the ring depth of the
-// persistent ring kernel (default, 3 stages), JO_QKR_EL=8 its 8-element lanes.
+// persistent ring kernel (default, 3 stages); JO_QKR_EL=16 selects 16-element
+// lanes (8 is the default), used only when cos/sin are 16-byte aligned.
 static int env_int(const char* name, int dflt) {
   const char* e = getenv(name);
   return e ? atoi(e) : dflt;

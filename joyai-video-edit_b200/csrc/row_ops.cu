@@ -441,23 +441,28 @@ void launch_rows(const RowArgs& a, int team, cudaStream_t st) {
   const int nvec = a.N / (16 / (int)sizeof(T));
   const int ntab = OP == OP_QUANT ? 0 : (MODROW || OP == OP_RMSNORM) ? 2 : 4;
   const size_t smem = (size_t)ntab * nvec * 16;
-  static bool attr_set = false;
-  if (!attr_set) {
+  struct Cache {
+    bool attr_set;
+    int cta, blocks;
+    size_t smem;
+  };
+  static Cache cache[kMaxDevices] = {};
+  Cache& c = cache[device_slot()];
+  if (!c.attr_set) {
     cudaFuncSetAttribute(row_kernel<T, OP, NORM, VPL, MODROW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          16 * 2048 * 4);
-    attr_set = true;
+    c.attr_set = true;
+    c.cta = -1;
   }
-  static int cached_cta = -1, cached_blocks = 0;
-  static size_t cached_smem = 0;
-  if (cached_cta != cta || cached_smem != smem) {
+  if (c.cta != cta || c.smem != smem) {
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_kernel<T, OP, NORM, VPL, MODROW>, cta, smem);
-    cached_blocks = (per_sm > 0 ? per_sm : 1) * sm_count();
-    cached_cta = cta;
-    cached_smem = smem;
+    c.blocks = (per_sm > 0 ? per_sm : 1) * sm_count();
+    c.cta = cta;
+    c.smem = smem;
   }
   const int64_t need = (a.M + rows_per_cta - 1) / rows_per_cta;
-  const int64_t grid = need < cached_blocks ? need : cached_blocks;
+  const int64_t grid = need < c.blocks ? need : c.blocks;
   row_kernel<T, OP, NORM, VPL, MODROW><<<(unsigned)grid, cta, smem, st>>>(a, team, rows_per_cta);
 }
 

@@ -576,11 +576,12 @@ int launch(const Args& a, int team, cudaStream_t st) {
   while (teams > 1 && tab + teams * per_team > 224 * 1024) --teams;
   const size_t smem = tab + teams * per_team;
   if (smem > 224 * 1024) return JO_ERR_INVALID;
-  static size_t attr = 0;
-  if (attr < smem) {
+  static size_t attr[kMaxDevices] = {};
+  size_t& opted = attr[device_slot()];
+  if (opted < smem) {
     cudaFuncSetAttribute(staged_rows<T, OP, NORM, VPL, S, R, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    attr = smem;
+    opted = smem;
   }
   const int64_t need = ((a.M + R - 1) / R + teams - 1) / teams;
   const int64_t grid = need < sm_count() ? need : sm_count();

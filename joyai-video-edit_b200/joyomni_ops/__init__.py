@@ -370,12 +370,13 @@ def fp8_scaled_mm_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, re
 
 
 def fp8_scaled_mm_scatter(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, dst_ptrs, parts, ranks,
-                          heads_per_rank, head_dim, tok0):
+                          heads_per_rank, head_dim, tok0, dst_tokens):
     """fp8_scaled_mm whose epilogue scatters the [M, parts*ranks*heads_per_rank*
     head_dim] result by head: row m, head h of part p goes to token tok0 + m,
     local head h % heads_per_rank of the [tokens, heads_per_rank, head_dim]
     buffer at dst_ptrs[p * ranks + h // heads_per_rank] (device addresses; a
-    peer rank's buffer through joyomni_stack.peer).  The sequence-parallel
+    peer rank's buffer through joyomni_stack.peer).  Every destination holds
+    dst_tokens token rows; tok0 + M must not exceed it.  The sequence-parallel
     all-to-all after the QKV projection, fused into the GEMM (new entry)."""
     if not has_fp8():
         raise NotImplementedError("joyomni_b200 was built without the FP8 GEMM")
@@ -384,6 +385,7 @@ def fp8_scaled_mm_scatter(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, dst
     N = mat_b.size(1)
     _chk(len(dst_ptrs) == parts * ranks, "dst_ptrs must hold parts * ranks addresses")
     _chk(N == parts * ranks * heads_per_rank * head_dim, "N must equal parts * ranks * heads_per_rank * head_dim")
+    _chk(0 <= tok0 and tok0 + M <= dst_tokens, "rows tok0 .. tok0 + M must fit the destinations' dst_tokens rows")
     lda = mat_a.stride(0) if M > 1 else K
     ldb = mat_b.stride(1) if N > 1 else K
     _chk(lda == K and ldb == K, "mat_a rows and mat_b columns must be densely packed")
@@ -392,7 +394,27 @@ def fp8_scaled_mm_scatter(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, dst
         _check(_L.jo_fp8_scaled_mm_scatter(
             mat_a.data_ptr(), mat_b.data_ptr(), scales_a.data_ptr(), scales_b.data_ptr(),
             bias.data_ptr() if bias is not None else None, M, N, K, _DT[out_dtype], arr, parts, ranks,
-            heads_per_rank, head_dim, tok0, st))
+            heads_per_rank, head_dim, tok0, dst_tokens, st))
+
+
+def check_gemm_fault(device=None) -> None:
+    """Raise RuntimeError if a GEMM on `device` (default: the current one) gave
+    up on a bounded wait since the last check, and clear the code.  The code is
+    one sticky value per device shared by every GEMM launch, so a non-zero
+    value means some launch since the last check returned incomplete output.
+    Synchronises the device; call it at a point that already synchronises
+    (end of a chunk, end of a benchmark phase)."""
+    if not has_fp8():
+        return
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        torch.cuda.synchronize(dev)
+        code = _L.jo_gemm_last_fault(1)
+    if code < 0:
+        _check(code)
+    if code != 0:
+        raise RuntimeError(f"fp8_scaled_mm: a GEMM launch timed out waiting on its pipeline (fault code {code}); "
+                           "its output is incomplete")
 
 
 from . import _torch_ops  # noqa: E402,F401  (registers torch.ops.joyomni_ops.*)

@@ -56,7 +56,8 @@ SIGNATURES = {
     "jo_fp8_scaled_mm": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
     "jo_fp8_scaled_mm_ex": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p, _p, _p],
     "jo_gemm_last_fault": [_i32],
-    "jo_fp8_scaled_mm_scatter": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _p, _i32, _i32, _i32, _i32, _i64, _p],
+    "jo_fp8_scaled_mm_scatter": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _p, _i32, _i32, _i32, _i32, _i64, _i64,
+                                 _p],
     "jo_ipc_get_handle": [_p, _p, ctypes.POINTER(_i64)],
     "jo_ipc_open": [_p, ctypes.POINTER(_p)],
     "jo_ipc_close": [_p],

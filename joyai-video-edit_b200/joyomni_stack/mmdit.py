@@ -97,11 +97,11 @@ class Fp8Weight:
         f = jo.fp8_scaled_mm_gelu if gelu else jo.fp8_scaled_mm
         return f(xq, self.t, xs, self.scale, torch.bfloat16, self.b, out=out)
 
-    def scatter(self, xq, xs, dst_ptrs, ranks, heads_per_rank, head_dim, tok0):
+    def scatter(self, xq, xs, dst_ptrs, ranks, heads_per_rank, head_dim, tok0, dst_tokens):
         """QKV projection with the sequence-parallel all-to-all in its epilogue:
         every (token, head) is stored in the owning rank's q / k / v buffer."""
         jo.fp8_scaled_mm_scatter(xq, self.t, xs, self.scale, torch.bfloat16, self.b, dst_ptrs, 3, ranks,
-                                 heads_per_rank, head_dim, tok0)
+                                 heads_per_rank, head_dim, tok0, dst_tokens)
 
     def residual(self, xq, xs, res, gate, out=None):
         """res + gate * (x @ W + b), gated residual fused in the GEMM epilogue."""
@@ -148,6 +148,8 @@ class LayerKV:
                                                      device=device)
         self.v = v if v is not None else torch.empty_like(self.k)
         self.peer = None        # PeerExchange of the layer (P > 1, peer mode)
+        self.keep_q = False     # tests: keep the last forward's head-sharded q in .last_q
+        self.last_q = None
         self.valid = 0          # cached image tokens
         self.next_slot = 0
         self.cur = sp.total_len
@@ -221,6 +223,8 @@ class Block:
         q = v5[0, :, 0] if sp.world == 1 else sp.seq_to_heads(v5[0, :, 0])     # strided view when P = 1
         sp.seq_to_heads(v5[0, :, 1], out=kv.k[:kv.cur])
         sp.seq_to_heads(v5[0, :, 2], out=kv.v[:kv.cur])
+        if kv.keep_q:
+            kv.last_q = q.clone()
         k_all, v_all = kv.keys()
         with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
                                              torch.nn.attention.SDPBackend.FLASH_ATTENTION,
@@ -245,9 +249,9 @@ class Block:
         Li = img.shape[0]
         ex = kv.peer
         xq, xs = norm_mod_quant(img, im[0], im[1])
-        self.img.qkv.scatter(xq, xs, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0])
+        self.img.qkv.scatter(xq, xs, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0], ex.q.shape[0])
         tq, ts = norm_mod_quant(txt, tm[0], tm[1])
-        self.txt.qkv.scatter(tq, ts, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0] + Li)
+        self.txt.qkv.scatter(tq, ts, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0] + Li, ex.q.shape[0])
         if ex.region is not None:
             ex.region.sync()
         q = ex.q
@@ -257,6 +261,8 @@ class Block:
             if nt:
                 jo.qk_norm_rope_strided(q[off + ni:off + ni + nt][None], kv.k[off + ni:off + ni + nt][None],
                                         NORM_EPS, self.txt.q_norm, self.txt.k_norm)
+        if kv.keep_q:
+            kv.last_q = q.clone()
         k_all, v_all = kv.keys()
         with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
                                              torch.nn.attention.SDPBackend.FLASH_ATTENTION,
@@ -442,4 +448,5 @@ class Stack:
             v = self._step(x.to(torch.bfloat16), txt, self.timestep_vec(t))
             x = x + (sig[i + 1] - sig[i]) * v.float()
         self.commit_kv()
+        jo.check_gemm_fault(self.device)     # a GEMM that gave up on a wait returned partial output
         return x

@@ -16,10 +16,31 @@ wheel is used instead (unpinned).  Set ``JO_REF_NO_FP8=1`` to build without it.
 """
 import os
 import sys
+import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REF = os.environ.get("JO_REF_ROOT", "/root/reference/deploy/joyomni_ops")
+
+
+def reference_root():
+    """Root of the reference checkout: $JO_REFERENCE_ROOT, else the
+    `reference_path` that BASELINE.json at the repository root records; None
+    when neither names an existing directory (the reference is then absent,
+    as on a GPU box, and nothing is built)."""
+    root = os.environ.get("JO_REFERENCE_ROOT")
+    if not root:
+        try:
+            import json
+            root = json.load(open(os.path.join(os.path.dirname(HERE), "BASELINE.json"))).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(root) else None
+
+
+def ops_dir():
+    root = reference_root()
+    d = os.path.join(root, "deploy", "joyomni_ops") if root else None
+    return d if d and os.path.isdir(d) else None
 
 
 def _cutlass_dir():
@@ -32,8 +53,9 @@ def _cutlass_dir():
 
 
 def build(no_fp8=None, verbose=False):
-    if not os.path.isdir(REF):
-        raise FileNotFoundError(f"reference sources not found at {REF}")
+    REF = ops_dir()
+    if REF is None:
+        raise FileNotFoundError("reference sources not found (set JO_REFERENCE_ROOT)")
     from torch.utils.cpp_extension import load
     if no_fp8 is None:
         no_fp8 = os.environ.get("JO_REF_NO_FP8", "") == "1"
@@ -58,6 +80,11 @@ def build(no_fp8=None, verbose=False):
         srcs += ["csrc/per_token_quant_fp8.cu", "csrc/fp8_gemm.cu"]
         name = "joyomni_ref"
     os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 4))
+    # torch's extension builder waits forever on a lock file left by a build
+    # that was killed; a lock older than an hour cannot belong to a live build.
+    lock = os.path.join(OUT, "lock")
+    if os.path.exists(lock) and time.time() - os.path.getmtime(lock) > 3600:
+        os.remove(lock)
     load(name=name, sources=[os.path.join(REF, s) for s in srcs],
          extra_include_paths=inc, extra_cflags=cflags, extra_cuda_cflags=flags,
          build_directory=OUT, is_python_module=False, verbose=verbose)

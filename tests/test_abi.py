@@ -1,6 +1,7 @@
 """CPU checks of the drop-in boundary: the C-ABI library loads and exports every
 symbol include/*.h declares, and the Python shim validates arguments with the
 reference's messages (no kernel is launched; there is no GPU here)."""
+import ctypes
 import glob
 import os
 import re
@@ -58,6 +59,11 @@ def test_invalid_arguments_rejected_before_any_launch():
     assert L.jo_fused_qk_norm_rope_3d_paired(None, None, 1, 2, 2, 96, 1e-6, None, None, None, None,
                                              None) == _lib.JO_ERR_INVALID
     assert "head_dim" in _lib.last_error()
+    # scatter rows beyond the destinations' token count (a peer GPU's buffer) are refused
+    dst = (ctypes.c_void_p * 3)(16, 16, 16)
+    assert L.jo_fp8_scaled_mm_scatter(16, 16, 16, 16, None, 8, 96, 64, _lib.JO_DTYPE_BF16, dst, 3, 1, 1, 32,
+                                      4, 10, None) == _lib.JO_ERR_INVALID
+    assert "do not fit" in _lib.last_error()
 
 
 def test_status_mapping():

@@ -159,7 +159,7 @@ def test_fp8_scaled_mm_scatter_emulated_ranks(jo, cuda, M, ranks, hpr, dh, tok0)
     dst = [torch.full((T, hpr, dh), -7.0, dtype=torch.bfloat16, device=cuda) for _ in range(parts * ranks)]
     jo.fp8_scaled_mm_scatter(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), torch.bfloat16,
                              torch.from_numpy(bias).to(torch.bfloat16).to(cuda), [d.data_ptr() for d in dst],
-                             parts, ranks, hpr, dh, tok0)
+                             parts, ranks, hpr, dh, tok0, T)
     torch.cuda.synchronize()
     want = ref.view(M, parts, ranks, hpr, dh)
     for p in range(parts):
@@ -176,6 +176,8 @@ def test_fp8_scaled_mm_scatter_rejects_bad_layout(jo, cuda):
     sb = torch.ones(96, device=cuda)
     d = torch.empty((4, 1, 32), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(RuntimeError):
-        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 3, 3, 1, 2, 32, 0)
+        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 3, 3, 1, 2, 32, 0, 4)
     with pytest.raises(RuntimeError):
-        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 2, 3, 1, 1, 32, 0)
+        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 2, 3, 1, 1, 32, 0, 4)
+    with pytest.raises(RuntimeError, match="must fit"):     # rows 1..5 overflow 4-token destinations
+        jo.fp8_scaled_mm_scatter(a, b, sa, sb, torch.bfloat16, None, [d.data_ptr()] * 3, 3, 1, 1, 32, 1, 4)

@@ -151,6 +151,26 @@ int jo_fp8_scaled_mm_ex(const void* mat_a, const void* mat_b, const float* scale
                         const void* bias, void* out, int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue,
                         const void* residual, const void* gate, void* stream);
 
+/*
+ * Multi-head attention forward, non-causal and unmasked, on the tcgen05
+ * tensor cores: out = softmax(scale * q k^T) v per (batch, head), fp32 scores
+ * and accumulators, bf16 in and out.  Replaces the reference block's external
+ * attention call, _flash_attention4 / _sdpa_attention
+ *   (deploy/xvideo/models/dit/dit.py:150-178, called at dit.py:419).
+ * Layout NHD as there: q [batch, Lq, heads, head_dim], k and v [batch, Lk,
+ * heads, head_dim], out [batch, Lq, heads, head_dim]; each *_strides array
+ * holds the batch, token and head strides in elements (multiples of 8; the
+ * head_dim elements of a row are contiguous).  head_dim == 128, dtype
+ * JO_DTYPE_BF16, Lk >= 1, 16-byte aligned tensors.
+ */
+int jo_attention_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t Lq, int64_t Lk,
+                     int64_t heads, int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, const int64_t* o_strides, float scale, int dtype, void* stream);
+
+/* Diagnostic: fault code left by an attention wait that timed out (0 = none);
+ * reset != 0 clears it.  Synchronous; for tests and end-of-chunk checks. */
+int jo_attention_last_fault(int reset);
+
 /* Diagnostic: fault code left by a GEMM wait that timed out (0 = none);
  * reset != 0 clears it.  Synchronous; for tests. */
 int jo_gemm_last_fault(int reset);

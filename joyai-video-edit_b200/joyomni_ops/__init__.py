@@ -12,14 +12,16 @@ on a non-sm_100 device, as TORCH_CHECK_NOT_IMPLEMENTED does).
 Extra entry points with no reference counterpart:
   * ``norm_modulate_quant_fp8`` — norm -> adaLN modulate -> per-token FP8 in one pass;
   * ``fp8_scaled_mm_gelu``      — FP8 GEMM with the GELU-tanh epilogue fused;
+  * ``attention``               — tcgen05 attention forward over NHD bf16 tensors
+    (the reference model's external FA4 / SDPA call, dit.py:150-178);
   * broadcast modulation in ``fused_norm_scale_shift``: scale/shift given as an
     expanded view (row stride 0) are read in place instead of being materialised.
 """
 from __future__ import annotations
 
-from typing import Optional
-
 import ctypes
+import math
+from typing import Optional
 
 import torch
 
@@ -37,6 +39,7 @@ __all__ = [
     "fp8_scaled_mm_gelu",
     "qk_norm_rope_strided",
     "fp8_scaled_mm_residual",
+    "attention",
 ]
 
 _DT = {torch.float32: _lib.JO_DTYPE_F32, torch.float16: _lib.JO_DTYPE_F16, torch.bfloat16: _lib.JO_DTYPE_BF16}
@@ -398,23 +401,61 @@ def fp8_scaled_mm_scatter(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, dst
 
 
 def check_gemm_fault(device=None) -> None:
-    """Raise RuntimeError if a GEMM on `device` (default: the current one) gave
-    up on a bounded wait since the last check, and clear the code.  The code is
-    one sticky value per device shared by every GEMM launch, so a non-zero
-    value means some launch since the last check returned incomplete output.
-    Synchronises the device; call it at a point that already synchronises
-    (end of a chunk, end of a benchmark phase)."""
-    if not has_fp8():
-        return
+    """Raise RuntimeError if a GEMM or attention launch on `device` (default:
+    the current one) gave up on a bounded wait since the last check, and clear
+    the codes.  Each kernel family keeps one sticky code per device shared by
+    all its launches, so a non-zero value means some launch since the last
+    check returned incomplete output.  Synchronises the device; call it at a
+    point that already synchronises (end of a chunk, end of a benchmark phase)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with torch.cuda.device(dev):
         torch.cuda.synchronize(dev)
-        code = _L.jo_gemm_last_fault(1)
-    if code < 0:
-        _check(code)
-    if code != 0:
-        raise RuntimeError(f"fp8_scaled_mm: a GEMM launch timed out waiting on its pipeline (fault code {code}); "
-                           "its output is incomplete")
+        codes = {"fp8_scaled_mm": _L.jo_gemm_last_fault(1) if has_fp8() else 0,
+                 "attention": _L.jo_attention_last_fault(1)}
+    for name, code in codes.items():
+        if code < 0:
+            _check(code)
+        if code != 0:
+            raise RuntimeError(f"{name}: a launch timed out waiting on its pipeline (fault code {code}); "
+                               "its output is incomplete")
+
+
+# --------------------------------------------------------------------------
+# attention  (replaces dit.py:150-178: FA4 / SDPA over NHD tensors)
+# --------------------------------------------------------------------------
+def attention(query, key, value, *, out=None, scale: Optional[float] = None):
+    """softmax(scale * q k^T) v, non-causal, for bf16 NHD tensors q [B, Lq, H, 128],
+    k and v [B, Lk, H, 128] (the layout of the reference's _flash_attention4,
+    deploy/xvideo/models/dit/dit.py:161-178); returns [B, Lq, H, 128] bf16 (or
+    writes `out`).  3-D [L, H, 128] views are taken as batch 1.  Any strides
+    whose last dimension is contiguous and whose others are multiples of 8
+    elements are read in place.  scale defaults to 1/sqrt(128)."""
+    squeeze = query.dim() == 3
+    q, k, v = (t.unsqueeze(0) if t.dim() == 3 else t for t in (query, key, value))
+    for name, t in (("query", q), ("key", k), ("value", v)):
+        _chk(t.is_cuda, f"{name} must be a CUDA tensor")
+        _chk(t.dim() == 4, f"{name} must be [B, L, H, D]")
+        _chk(t.dtype == torch.bfloat16, f"{name} must be BFloat16")
+        _chk(t.size(3) == 128 and t.stride(3) == 1, f"{name} must have a contiguous head_dim of 128")
+    B, Lq, H, Dh = q.shape
+    _chk(k.shape[0] == B and v.shape[0] == B and k.shape[2] == H and v.shape[2] == H, "batch / heads mismatch")
+    _chk(k.shape[1] == v.shape[1], "key and value lengths differ")
+    if out is None:
+        o = torch.empty((B, Lq, H, Dh), dtype=torch.bfloat16, device=q.device)
+    else:
+        o = out.unsqueeze(0) if out.dim() == 3 else out
+        _chk(o.shape == (B, Lq, H, Dh) and o.dtype == torch.bfloat16 and o.stride(3) == 1,
+             "out must be a [B, Lq, H, 128] bf16 tensor")
+    sc = (1.0 / math.sqrt(Dh)) if scale is None else float(scale)
+
+    def strides(t):
+        return (ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2))
+    with _Device(q) as st:
+        _check(_L.jo_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, Lq, k.shape[1], H, Dh,
+                                   strides(q), strides(k), strides(v), strides(o), sc, _lib.JO_DTYPE_BF16, st))
+    if out is not None:
+        return out
+    return o[0] if squeeze else o
 
 
 from . import _torch_ops  # noqa: E402,F401  (registers torch.ops.joyomni_ops.*)

@@ -371,27 +371,42 @@ def stack_bench(torch, dev, world):
         return ms
 
     blk = lambda: st.blocks[0].forward(xb, txt, vec, st.cos, st.sin, st.kv[0], st.sp)  # noqa: E731
-    blk()
-    blk()
-    block_ms = timed(blk, 5)
+    block_ms = {}
+    for backend in ("joyomni", "sdpa"):
+        st.cfg.attention = backend
+        blk()
+        blk()
+        block_ms[backend] = timed(blk, 5)
+    st.cfg.attention = "joyomni"
     state = {"x": st.denoise_chunk(x, txt)}          # warm chunk (cache stays full: commit rotates slots)
 
     def chunk():
         state["x"] = st.denoise_chunk(state["x"], txt)
     chunk_ms_eager = timed(chunk, 1)
-    graph = st.capture(txt)                           # whole 40-layer step in one CUDA graph
-    chunk()
-    chunk_ms = timed(chunk, 1) if graph else chunk_ms_eager
+    chunk_ms, graphs = {}, {}
+    for backend in ("joyomni", "sdpa"):
+        st.cfg.attention = backend
+        graphs[backend] = st.capture(txt)             # whole 40-layer step in one CUDA graph
+        chunk()
+        chunk_ms[backend] = timed(chunk, 1) if graphs[backend] else (chunk_ms_eager if backend == "joyomni" else None)
+    st.cfg.attention = "joyomni"
+    graph = graphs["joyomni"]
     finite = bool(torch.isfinite(state["x"]).all())
     gflop_block = 2 * (cfg.img_tokens + cfg.txt_tokens) * cfg.hidden * (4 * cfg.hidden + 2 * cfg.ffn) / 1e9
     attn_flop = 4 * (cfg.img_tokens + cfg.txt_tokens) * (cfg.img_tokens * 3 + cfg.txt_tokens) * cfg.hidden / 1e9
+    cms = chunk_ms["joyomni"]
     out = {"config": "cfg4 block / cfg5 40 layers x 3 steps, 10530 img + 512 txt tokens, KV 2 chunks (post-RoPE)",
-           "ulysses_degree": world, "block_ms": round(block_ms, 2), "chunk_ms": round(chunk_ms, 1),
+           "ulysses_degree": world, "block_ms": round(block_ms["joyomni"], 2), "chunk_ms": round(cms, 1),
            "chunk_ms_eager": round(chunk_ms_eager, 1), "step_cuda_graph": graph,
            **({} if graph else {"capture_error": getattr(st, "capture_error", "")}),
-           "fps": round(24 / (chunk_ms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
+           "fps": round(24 / (cms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
            "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
-           "attention": "torch SDPA (cuDNN/flash), bf16",
+           "attention": "joyomni_ops.attention (tcgen05 kernel of this repository), bf16",
+           "with_torch_sdpa_attention": {"block_ms": round(block_ms["sdpa"], 2),
+                                         "chunk_ms": None if chunk_ms["sdpa"] is None else round(chunk_ms["sdpa"], 1),
+                                         "fps": None if chunk_ms["sdpa"] is None else
+                                         round(24 / (chunk_ms["sdpa"] / 1e3), 2),
+                                         "attention": "torch SDPA (cuDNN), bf16"},
            "sp_exchange": ("NCCL all_to_all" if st.region is None else
                            "q/k/v stored by head straight into the q buffer and K/V cache by the QKV GEMM "
                            "epilogue" if world == 1 else
@@ -455,9 +470,34 @@ def kernel_table(torch, jo, dev):
     out["k3_rmsnorm_421200x128"] = _kline(2 * kxs[0].numel() * 2 + 256, ms / 10, pk)
     del kxs
 
+    out.update(attention_table(torch, jo, dev, pk))
     if jo.has_fp8():
         out.update(gemm_table(torch, jo, dev, gen))
     return out
+
+
+def attention_table(torch, jo, dev, pk):
+    """Config 4's attention at P = 1: 10530 + 512 queries over 2 x 10530 cached +
+    11042 current keys, 40 heads x 128, bf16 (4 * Lq * Lk * H * 128 FLOP); this
+    repository's tcgen05 kernel against torch's cuDNN SDPA on the same inputs."""
+    import torch.nn.functional as F
+    Lq, Lk, H = 11042, 32102, 40
+    g = torch.Generator(device=dev).manual_seed(4)
+    q = torch.randn(Lq, H, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(Lk, H, 128, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(Lk, H, 128, generator=g, device=dev).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    fl = 4.0 * Lq * Lk * H * 128
+    ms, _ = graph_time(torch, [lambda: jo.attention(q, k, v, out=o) for _ in range(3)], 5)
+    with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION]):
+        ms_ref, _ = graph_time(torch, [lambda: F.scaled_dot_product_attention(
+            q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None], v.permute(1, 0, 2)[None]) for _ in range(3)], 5)
+    jo.check_gemm_fault(dev)
+    t, t_ref = ms / 3 * 1e-3, ms_ref / 3 * 1e-3
+    return {"cfg4_attention": {"us": round(t * 1e6, 1), "tflops": round(fl / t / 1e12, 1),
+                               "frac_of_measured_bf16_burst": round(fl / t / (1e12 * pk["bf16_tflops"]), 4),
+                               "torch_cudnn_sdpa_us": round(t_ref * 1e6, 1),
+                               "torch_cudnn_sdpa_tflops": round(fl / t_ref / 1e12, 1)}}
 
 
 def gemm_table(torch, jo, dev, gen):

@@ -10,7 +10,8 @@ random-initialised weights and synthetic inputs.  Per block and stream:
   qkv  = fp8_scaled_mm(x_q, W_qkv) + b                                          (fp8_linear.py:167)
   q, k = RMSNorm_head + 3D RoPE, in place in the qkv buffer (image stream);     (dit.py:364-370)
          RMSNorm_head only (text stream)                                        (dit.py:384-385)
-  attn = SDPA(q_img|q_txt, [k_cache | k_img | k_txt], [v ...])                   (dit.py:387-420)
+  attn = attention(q_img|q_txt, [k_cache | k_img | k_txt], [v ...])              (dit.py:387-420)
+         (tcgen05 kernel of this repository, or torch SDPA with cfg.attention = "sdpa")
   x    = x + gate1 * fp8_linear(attn, W_proj)     residual in the GEMM epilogue  (dit.py:463-466)
   x    = x + gate2 * fp8_linear(gelu_tanh(fp8_linear(mod2(LN(x)), W_up)), W_down)  (dit.py:467-476)
          (GELU in the up-projection epilogue, gated residual in the down-projection epilogue)
@@ -27,7 +28,7 @@ from __future__ import annotations
 
 import math
 import os
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import List, Optional
 
 import torch
@@ -54,6 +55,9 @@ class StackConfig:
     rope_theta: float = 10000.0
     cache_chunks: int = 2
     seed: int = 5
+    # attention kernel: "joyomni" (tcgen05 kernel of this repository) or "sdpa"
+    # (torch cuDNN / flash); JOYOMNI_ATTENTION overrides the default
+    attention: str = field(default_factory=lambda: os.environ.get("JOYOMNI_ATTENTION", "joyomni"))
 
     @property
     def head_dim(self) -> int:
@@ -106,6 +110,21 @@ class Fp8Weight:
     def residual(self, xq, xs, res, gate, out=None):
         """res + gate * (x @ W + b), gated residual fused in the GEMM epilogue."""
         return jo.fp8_scaled_mm_residual(xq, self.t, xs, self.scale, torch.bfloat16, self.b, res, gate, out=out)
+
+
+def attend(q, k, v, backend: str):
+    """Non-causal attention of head-sharded q [Lq, h, 128] over k, v [Lk, h, 128]
+    (the block's FA4 / SDPA call, dit.py:150-178, 419), returning [Lq, h, 128].
+    backend "joyomni": this repository's tcgen05 kernel (joyomni_ops.attention,
+    strided views read in place); "sdpa": torch SDPA (cuDNN / flash), bf16."""
+    if backend == "joyomni":
+        return jo.attention(q, k, v)
+    with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
+                                         torch.nn.attention.SDPBackend.FLASH_ATTENTION,
+                                         torch.nn.attention.SDPBackend.EFFICIENT_ATTENTION]):
+        o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None],
+                                           v.permute(1, 0, 2)[None])
+    return o[0].permute(1, 0, 2)
 
 
 def quant(x):
@@ -226,12 +245,7 @@ class Block:
         if kv.keep_q:
             kv.last_q = q.clone()
         k_all, v_all = kv.keys()
-        with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
-                                             torch.nn.attention.SDPBackend.FLASH_ATTENTION,
-                                             torch.nn.attention.SDPBackend.EFFICIENT_ATTENTION]):
-            o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k_all.permute(1, 0, 2)[None],
-                                               v_all.permute(1, 0, 2)[None])
-        o = sp.heads_to_seq(o[0].permute(1, 0, 2)).reshape(Li + Lt, D)
+        o = sp.heads_to_seq(attend(q, k_all, v_all, cfg.attention)).reshape(Li + Lt, D)
 
         # ---- projections + FFN with gated residuals ------------------------
         img = self._tail(self.img, im, img, o[:Li])
@@ -264,12 +278,7 @@ class Block:
         if kv.keep_q:
             kv.last_q = q.clone()
         k_all, v_all = kv.keys()
-        with torch.nn.attention.sdpa_kernel([torch.nn.attention.SDPBackend.CUDNN_ATTENTION,
-                                             torch.nn.attention.SDPBackend.FLASH_ATTENTION,
-                                             torch.nn.attention.SDPBackend.EFFICIENT_ATTENTION]):
-            o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k_all.permute(1, 0, 2)[None],
-                                               v_all.permute(1, 0, 2)[None])
-        o = sp.heads_to_seq(o[0].permute(1, 0, 2)).reshape(Li + txt.shape[0], D)
+        o = sp.heads_to_seq(attend(q, k_all, v_all, self.cfg.attention)).reshape(Li + txt.shape[0], D)
         img = self._tail(self.img, im, img, o[:Li])
         txt = self._tail(self.txt, tm, txt, o[Li:])
         return img, txt

@@ -47,7 +47,18 @@ def qk_norm(x, w, cos=None, sin=None):
     return e.to(torch.bfloat16)
 
 
-def block_forward(blk, img, txt, vec, cos, sin, cache_k=None, cache_v=None):
+def attention_fp32(q, k, v):
+    """softmax(q k^T / sqrt(d)) v in fp32, one head at a time; q [Lq, H, D], k/v [Lk, H, D]."""
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    sc = 1.0 / (q.shape[-1] ** 0.5)
+    for h in range(q.shape[1]):
+        p = torch.softmax((q[:, h].float() @ k[:, h].float().t()) * sc, dim=-1)
+        out[:, h] = p @ v[:, h].float()
+        del p
+    return out
+
+
+def block_forward(blk, img, txt, vec, cos, sin, cache_k=None, cache_v=None, attn="sdpa"):
     H, Dh, D = blk.cfg.heads, blk.cfg.head_dim, blk.cfg.hidden
     Li = img.shape[0]
     im = (blk.img.mod + vec).unbind(0)
@@ -60,9 +71,12 @@ def block_forward(blk, img, txt, vec, cos, sin, cache_k=None, cache_v=None):
     if cache_k is not None:
         k = torch.cat((k, cache_k), 0)
         v = torch.cat((v, cache_v), 0)
-    # bf16 attention, as the reference model runs it (FA4 / SDPA in bf16, dit.py:162-178)
-    o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None],
-                                       v.permute(1, 0, 2)[None])[0].permute(1, 0, 2)
+    if attn == "fp32":
+        o = attention_fp32(q, k, v)
+    else:
+        # bf16 attention, as the reference model runs it (FA4 / SDPA in bf16, dit.py:162-178)
+        o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None],
+                                           v.permute(1, 0, 2)[None])[0].permute(1, 0, 2)
     o = o.reshape(-1, D).to(torch.bfloat16)
 
     def tail(st, m, x, attn):

@@ -13,7 +13,8 @@ shapes):
   norm tolerance of the oracle;
 * one MMDiT block at BASELINE config 4 dims (hidden 5120, 40 heads x 128, FFN
   13824, 10530 image + 512 text tokens, 21060 cached keys) against the eager
-  restatement of the reference block, relative RMS <= 1e-2.
+  restatement of the reference block, whole (bounded by the spread between
+  two valid attention kernels) and stage by stage.
 """
 import numpy as np
 import pytest
@@ -77,25 +78,84 @@ def test_headline_reference_api_chain(jo, cuda, cfg2):
     print(f"K2 -> K4 chain vs oracle chain: differing codes {float((codes_np(q) != oq).mean()):.3e}")
 
 
-def test_block_at_config4_dims(cuda):
-    import stack_reference as R
+@pytest.fixture(scope="module")
+def block4(cuda):
+    """One block at config-4 dims with a full 2-chunk cache (21060 keys) and its inputs."""
     from joyomni_stack import Stack, StackConfig
     cfg = StackConfig(layers=1)
     st = Stack(cfg, cuda)
     gen = torch.Generator(device=cuda).manual_seed(3)
     st.kv[0].fill_random(gen, cfg.cache_chunks)
     img, txt = st.inputs(7)
-    img = img.to(torch.bfloat16)
-    vec = st.timestep_vec(1000)
+    yield st, img.to(torch.bfloat16), txt, st.timestep_vec(1000)
+    st.close()
+
+
+def test_block_at_config4_dims(cuda, block4):
+    """The whole block against its eager restatement.  Any two valid bf16
+    attention kernels differ by bf16 rounding flips, which the per-token FP8
+    requantisations that follow amplify; the bound is therefore set by the
+    spread between two valid references: the restatement with torch's bf16
+    SDPA (the reference model's own fallback, dit.py:150-158) against the same
+    restatement with fp32 attention.  This repository's block (tcgen05
+    attention) must be at least as close to the fp32-attention restatement as
+    the SDPA one is (x1.25 + 1e-3); as a sanity bound, within 5e-2 of both
+    (measured: 2.6e-2 against fp32 attention, where SDPA sits at 2.55e-2, and
+    1.5e-2 against the SDPA restatement)."""
+    import stack_reference as R
+    st, img, txt, vec = block4
     kv = st.kv[0]
     assert kv.valid == 21060
     ck = kv.k[kv.cur: kv.cur + kv.valid].clone()
     cv = kv.v[kv.cur: kv.cur + kv.valid].clone()
+    st.cfg.attention = "joyomni"
     out_img, out_txt = st.blocks[0].forward(img, txt, vec, st.cos, st.sin, kv, st.sp)
+    out_img, out_txt = out_img.clone(), out_txt.clone()
     torch.cuda.synchronize()
-    ref_img, ref_txt, _, _ = R.block_forward(st.blocks[0], img, txt, vec, st.cos, st.sin, ck, cv)
-    ri, rt = rel_rms(to_np(out_img), to_np(ref_img)), rel_rms(to_np(out_txt), to_np(ref_txt))
-    print(f"\nconfig-4 block vs eager restatement: rel RMS img {ri:.3e} txt {rt:.3e}")
+    sd_img, sd_txt, _, _ = R.block_forward(st.blocks[0], img, txt, vec, st.cos, st.sin, ck, cv, attn="sdpa")
+    f_img, f_txt, _, _ = R.block_forward(st.blocks[0], img, txt, vec, st.cos, st.sin, ck, cv, attn="fp32")
+    e_ours = max(rel_rms(to_np(out_img), to_np(f_img)), rel_rms(to_np(out_txt), to_np(f_txt)))
+    e_sdpa = max(rel_rms(to_np(sd_img), to_np(f_img)), rel_rms(to_np(sd_txt), to_np(f_txt)))
+    e_vs_sdpa = max(rel_rms(to_np(out_img), to_np(sd_img)), rel_rms(to_np(out_txt), to_np(sd_txt)))
+    print(f"\nconfig-4 block rel RMS: ours vs fp32-attention restatement {e_ours:.3e}, SDPA restatement vs "
+          f"fp32-attention restatement {e_sdpa:.3e}, ours vs SDPA restatement {e_vs_sdpa:.3e}")
     assert torch.isfinite(out_img).all() and torch.isfinite(out_txt).all()
-    assert ri <= 1e-2 and rt <= 1e-2
-    st.close()
+    assert e_ours <= 1.25 * e_sdpa + 1e-3
+    assert e_ours <= 5e-2 and e_vs_sdpa <= 5e-2
+
+
+def test_block_stages_at_config4_dims(jo, cuda, block4):
+    """Stage by stage at config-4 dims, each stage fed the restatement's own
+    input so that nothing upstream is amplified: norm -> modulate -> FP8 codes,
+    the FP8 GEMMs with their fused epilogues (bias, GELU, gated residual)."""
+    import stack_reference as R
+    from joyomni_stack.mmdit import norm_mod_quant
+    st, img, txt, vec = block4
+    blk = st.blocks[0]
+    im = (blk.img.mod + vec).unbind(0)
+
+    def rel(a, b):
+        return rel_rms(to_np(a), to_np(b))
+    yref = R.ln_mod(img, im[0], im[1])
+    qr, sr = R.quant(yref)
+    xq, xs = norm_mod_quant(img, im[0], im[1])
+    code_frac = (xq.float() != qr).float().mean().item()
+    qkv_ref = R.lin(qr, sr, blk.img.qkv)
+    qkv = blk.img.qkv(qr.to(torch.float8_e4m3fn), sr.contiguous())
+    attn = torch.randn(img.shape[0], st.cfg.hidden, generator=torch.Generator(device=cuda).manual_seed(9),
+                       device=cuda).to(torch.bfloat16)
+    aq, as_ = R.quant(attn)
+    pr_ref = torch.addcmul(img, R.lin(aq, as_, blk.img.proj), im[2])
+    pr = blk.img.proj.residual(aq.to(torch.float8_e4m3fn), as_.contiguous(), img, im[2])
+    hq, hs = R.quant(R.ln_mod(pr_ref, im[3], im[4]))
+    up_ref = R.lin(hq, hs, blk.img.up, gelu=True)
+    up = blk.img.up(hq.to(torch.float8_e4m3fn), hs.contiguous(), gelu=True)
+    h2q, h2s = R.quant(up_ref)
+    dn_ref = torch.addcmul(pr_ref, R.lin(h2q, h2s, blk.img.down), im[5])
+    dn = blk.img.down.residual(h2q.to(torch.float8_e4m3fn), h2s.contiguous(), pr_ref.clone(), im[5])
+    res = {"norm_mod_quant_code_frac": code_frac, "qkv": rel(qkv, qkv_ref), "proj_resid": rel(pr, pr_ref),
+           "up_gelu": rel(up, up_ref), "down_resid": rel(dn, dn_ref)}
+    print("\nconfig-4 stages:", {k: f"{v:.2e}" for k, v in res.items()})
+    assert res["norm_mod_quant_code_frac"] <= 1e-4
+    assert res["qkv"] <= 1e-3 and res["proj_resid"] <= 1e-3 and res["down_resid"] <= 1e-3
+    assert res["up_gelu"] <= 2e-3

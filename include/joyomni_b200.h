@@ -152,6 +152,21 @@ int jo_fp8_scaled_mm_ex(const void* mat_a, const void* mat_b, const float* scale
                         const void* residual, const void* gate, void* stream);
 
 /*
+ * RoPE of bf16 keys with fp32 tables (the pre-RoPE KV-cache path: keys stored
+ * after the per-head RMSNorm and rotated at the positions they take in the
+ * attention window).  Replaces apply_rotary_emb on cached keys
+ *   (deploy/xvideo/models/dit/rope.py:21-28; callers dit.py:211-217 and
+ *    deploy/xvideo/serving/graph_runner.py:137-142), with that expression's
+ * fp32 roundings: o0 = RN(RN(x0*c) + RN(-x1*s)), o1 = RN(RN(x1*c) + RN(x0*s))
+ * per interleaved pair, then bf16.  x, out: [L, H, head_dim] bf16 with token /
+ * head strides (elements, multiples of 8); cos, sin: fp32 [L, head_dim/2].
+ * head_dim in {64, 128, 256}; out may alias x.
+ */
+int jo_rope_apply(void* out, const void* x, const float* cos, const float* sin, int64_t L, int64_t H,
+                  int64_t head_dim, int64_t x_token_stride, int64_t x_head_stride, int64_t out_token_stride,
+                  int64_t out_head_stride, void* stream);
+
+/*
  * Multi-head attention forward, non-causal and unmasked, on the tcgen05
  * tensor cores: out = softmax(scale * q k^T) v per (batch, head), fp32 scores
  * and accumulators, bf16 in and out.  Replaces the reference block's external

@@ -40,6 +40,7 @@ __all__ = [
     "qk_norm_rope_strided",
     "fp8_scaled_mm_residual",
     "attention",
+    "rope_apply",
 ]
 
 _DT = {torch.float32: _lib.JO_DTYPE_F32, torch.float16: _lib.JO_DTYPE_F16, torch.bfloat16: _lib.JO_DTYPE_BF16}
@@ -203,8 +204,9 @@ def fused_norm_scale_shift(x, gamma, beta, scale, shift, norm_type, eps=1e-5):
 # --------------------------------------------------------------------------
 # rmsnorm  (rmsnorm.cu:76-95)
 # --------------------------------------------------------------------------
-def rmsnorm(x, weight, eps=1e-6):
-    """(x / RMS(x)) * weight. x: [M, N], weight: [N]."""
+def rmsnorm(x, weight, eps=1e-6, *, out=None):
+    """(x / RMS(x)) * weight. x: [M, N], weight: [N].  `out` (keyword, an
+    extension): a dense [M, N] destination, e.g. rows of a preallocated buffer."""
     _check_cuda(x, "x")
     _check_cuda(weight, "weight")
     _chk(x.dim() == 2, "x must be 2D [M, N]")
@@ -215,7 +217,11 @@ def rmsnorm(x, weight, eps=1e-6):
         _fail("Unsupported dtype; use float32/float16/bfloat16")
     M, N = x.shape
     weight = weight.contiguous()
-    out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    else:
+        _chk(out.shape == (M, N) and out.dtype == x.dtype and out.is_cuda and out.is_contiguous(),
+             "out must be a dense [M, N] tensor of x's dtype")
     with _Device(x) as st:
         _check(_L.jo_rmsnorm(out.data_ptr(), x.data_ptr(), weight.data_ptr(), M, N,
                              x.stride(0) if M > 1 else N, float(eps), _DT[x.dtype], st))
@@ -418,6 +424,30 @@ def check_gemm_fault(device=None) -> None:
         if code != 0:
             raise RuntimeError(f"{name}: a launch timed out waiting on its pipeline (fault code {code}); "
                                "its output is incomplete")
+
+
+# --------------------------------------------------------------------------
+# rope_apply  (replaces rope.py:21-28 apply_rotary_emb on pre-RoPE cached keys)
+# --------------------------------------------------------------------------
+def rope_apply(x, cos, sin, *, out=None):
+    """RoPE of bf16 keys x [L, H, D] (token / head strides multiples of 8, last
+    dim contiguous) with fp32 tables cos, sin [L, D/2]: the arithmetic of
+    apply_rotary_emb (deploy/xvideo/models/dit/rope.py:21-28) as the pre-RoPE
+    KV-cache path applies it to cached keys.  Returns a new [L, H, D] tensor or
+    writes `out` (which may be x itself)."""
+    _chk(x.is_cuda and cos.is_cuda and sin.is_cuda, "x, cos and sin must be CUDA tensors")
+    _chk(x.dim() == 3 and x.dtype == torch.bfloat16 and x.stride(2) == 1, "x must be a [L, H, D] bf16 view")
+    L, H, D = x.shape
+    for t in (cos, sin):
+        _chk(t.dtype == torch.float32 and t.shape == (L, D // 2) and t.is_contiguous(),
+             "cos and sin must be contiguous fp32 [L, D/2]")
+    if out is None:
+        out = torch.empty((L, H, D), dtype=torch.bfloat16, device=x.device)
+    _chk(out.shape == x.shape and out.dtype == torch.bfloat16 and out.stride(2) == 1, "out must match x")
+    with _Device(x) as st:
+        _check(_L.jo_rope_apply(out.data_ptr(), x.data_ptr(), cos.data_ptr(), sin.data_ptr(), L, H, D,
+                                x.stride(0), x.stride(1), out.stride(0), out.stride(1), st))
+    return out
 
 
 # --------------------------------------------------------------------------

@@ -55,6 +55,7 @@ SIGNATURES = {
     "jo_norm_modulate_quant_fp8": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _p, _p, _p],
     "jo_fp8_scaled_mm": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
     "jo_fp8_scaled_mm_ex": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p, _p, _p],
+    "jo_rope_apply": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "jo_attention_fwd": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
                          ctypes.POINTER(_i64), ctypes.POINTER(_i64), _f32, _i32, _p],
     "jo_attention_last_fault": [_i32],

@@ -58,26 +58,34 @@ class StackConfig:
     # attention kernel: "joyomni" (tcgen05 kernel of this repository) or "sdpa"
     # (torch cuDNN / flash); JOYOMNI_ATTENTION overrides the default
     attention: str = field(default_factory=lambda: os.environ.get("JOYOMNI_ATTENTION", "joyomni"))
+    # KV cache of pre-RoPE keys (the reference's kv_cache_pre_rope=True,
+    # dit.py:360-363): keys are cached after the per-head RMSNorm only and
+    # rotated at their window positions when the cache is assembled.
+    kv_cache_pre_rope: bool = False
 
     @property
     def head_dim(self) -> int:
         return self.hidden // self.heads
 
 
-def rope_tables(cfg: StackConfig, device) -> tuple:
-    """cos/sin [T*H*W, head_dim/2] bf16 for the row-major (t, h, w) grid:
-    per axis f_j = 1/theta^(2j/d), angle = pos * f_j (fp32); the de-duplicated
-    half of the repeat_interleaved tables (rope.py:31-52, sgl_fused_ops.py:87-94)."""
+def rope_tables(cfg: StackConfig, device, t0: int = 0, fp32: bool = False) -> tuple:
+    """cos/sin [T*H*W, head_dim/2] for the row-major (t, h, w) grid with
+    temporal positions t0 .. t0+T-1: per axis f_j = 1/theta^(2j/d), angle =
+    pos * f_j (fp32); the de-duplicated half of the repeat_interleaved tables
+    (rope.py:31-52, sgl_fused_ops.py:87-94), rounded to bf16 for the fused
+    QK-norm + RoPE kernel, or kept in fp32 (fp32=True) for rotating cached
+    pre-RoPE keys (apply_rotary_emb's fp32 tables, dit.py:955-973)."""
     T, H, W = cfg.grid
-    tt, hh, ww = torch.meshgrid(torch.arange(T), torch.arange(H), torch.arange(W), indexing="ij")
+    tt, hh, ww = torch.meshgrid(torch.arange(T) + t0, torch.arange(H), torch.arange(W), indexing="ij")
     cs, sn = [], []
     for pos, d in zip((tt, hh, ww), cfg.rope_axes):
         f = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2)[: d // 2].float() / d))
         ang = torch.outer(pos.reshape(-1).float(), f)
         cs.append(ang.cos())
         sn.append(ang.sin())
-    return (torch.cat(cs, 1).to(torch.bfloat16).to(device).contiguous(),
-            torch.cat(sn, 1).to(torch.bfloat16).to(device).contiguous())
+    dt = torch.float32 if fp32 else torch.bfloat16
+    return (torch.cat(cs, 1).to(dt).to(device).contiguous(),
+            torch.cat(sn, 1).to(dt).to(device).contiguous())
 
 
 class Fp8Weight:
@@ -168,7 +176,16 @@ class LayerKV:
         self.v = v if v is not None else torch.empty_like(self.k)
         self.peer = None        # PeerExchange of the layer (P > 1, peer mode)
         self.keep_q = False     # tests: keep the last forward's head-sharded q in .last_q
-        self.last_q = None
+        self.last_q = None      # (and, on the peer / local exchange path, the raw keys in .last_k_raw)
+        self.last_k_raw = None
+        # pre-RoPE mode: normalised, unrotated keys of the cache slots (kpre) and
+        # of the current chunk's image tokens (stage, refreshed every forward)
+        self.pre_rope = cfg.kv_cache_pre_rope
+        self.kpre = torch.empty((self.cap, sp.local_heads, cfg.head_dim), dtype=torch.bfloat16, device=device) \
+            if self.pre_rope else None
+        self.stage = torch.empty((cfg.img_tokens, sp.local_heads, cfg.head_dim), dtype=torch.bfloat16,
+                                 device=device) if self.pre_rope else None
+        self.slot_age = []      # pre-RoPE mode: ring slots, oldest first
         self.valid = 0          # cached image tokens
         self.next_slot = 0
         self.cur = sp.total_len
@@ -178,24 +195,54 @@ class LayerKV:
         n = self.cur + self.valid
         return self.k[:n], self.v[:n]
 
-    def commit(self, sp: SeqParallel):
-        """Store the current chunk's image-token K/V into the ring (oldest slot)."""
+    def commit(self, sp: SeqParallel, tables=None):
+        """Store the current chunk's image-token K/V into the ring (oldest slot).
+        Pre-RoPE mode: the slot gets the normalised, unrotated keys of the stage
+        buffer, and every cached slot is re-rotated at its window position
+        (tables(age) -> fp32 cos/sin; see assemble)."""
         base = self.cur + self.next_slot * self.img_len
         off = 0
         for start, length in sp.gathered_img_segments():
-            self.k[base + off: base + off + length].copy_(self.k[start:start + length])
+            if not self.pre_rope:
+                self.k[base + off: base + off + length].copy_(self.k[start:start + length])
             self.v[base + off: base + off + length].copy_(self.v[start:start + length])
             off += length
+        if self.pre_rope:
+            s0 = self.next_slot * self.img_len
+            self.kpre[s0:s0 + self.img_len].copy_(self.stage)
+            if self.next_slot in self.slot_age:
+                self.slot_age.remove(self.next_slot)
+            self.slot_age.append(self.next_slot)
         self.next_slot = (self.next_slot + 1) % (self.cap // self.img_len)
         self.valid = min(self.cap, self.valid + self.img_len)
+        if self.pre_rope and tables is not None:
+            self.assemble(tables)
 
-    def fill_random(self, gen, chunks: int):
-        """Pre-fill `chunks` cache slots with N(0,1) K/V."""
+    def assemble(self, tables):
+        """Pre-RoPE mode: rotate every cached slot's keys at the position it
+        holds in the attention window, oldest slot at chunk position 0 (the
+        shifted temporal ids of the reference's cache assembly, dit.py:189-225,
+        955-973; graph_runner.py:137-142 rotates at commit the same way)."""
+        for age, slot in enumerate(self.slot_age):
+            c, s_ = tables(age)
+            r0 = slot * self.img_len
+            jo.rope_apply(self.kpre[r0:r0 + self.img_len], c, s_,
+                          out=self.k[self.cur + r0: self.cur + r0 + self.img_len])
+
+    def fill_random(self, gen, chunks: int, tables=None):
+        """Pre-fill `chunks` cache slots with N(0,1) K/V; in
+        pre-RoPE mode the unrotated keys, then rotated into the window."""
         n = chunks * self.img_len
-        self.k[self.cur:self.cur + n].normal_(generator=gen)
+        if self.pre_rope:
+            self.kpre[:n].normal_(generator=gen)
+            self.slot_age = list(range(chunks))
+        else:
+            self.k[self.cur:self.cur + n].normal_(generator=gen)
         self.v[self.cur:self.cur + n].normal_(generator=gen)
         self.valid = n
         self.next_slot = chunks % (self.cap // self.img_len)
+        if self.pre_rope and tables is not None:
+            self.assemble(tables)
 
 
 @dataclass
@@ -227,6 +274,8 @@ class Block:
 
         if kv.peer is not None:
             return self._forward_peer(img, txt, im, tm, kv, sp)
+        if kv.pre_rope:
+            raise NotImplementedError("the pre-RoPE KV cache needs the peer / local exchange (JOYOMNI_SP_EXCHANGE=peer)")
 
         # ---- QKV of both streams into one [L_local, 3, H, Dh] buffer --------
         qkv = torch.empty((Li + Lt, 3 * D), dtype=torch.bfloat16, device=img.device)
@@ -269,6 +318,14 @@ class Block:
         if ex.region is not None:
             ex.region.sync()
         q = ex.q
+        if kv.keep_q:
+            kv.last_k_raw = kv.k[:kv.cur].clone()
+        if kv.pre_rope:
+            # the normalised, unrotated keys of the image tokens (the reference's
+            # rmsnorm_qk_bf16 on img_k, dit.py:360-363), for the cache commit
+            for off, ni, nt, i0 in ex.seg:
+                jo.rmsnorm(kv.k[off:off + ni].reshape(-1, Dh), self.img.k_norm, NORM_EPS,
+                           out=kv.stage[i0:i0 + ni].view(-1, Dh))
         for off, ni, nt, i0 in ex.seg:
             jo.qk_norm_rope_strided(q[off:off + ni][None], kv.k[off:off + ni][None], NORM_EPS, self.img.q_norm,
                                     self.img.k_norm, ex.cos[i0:i0 + ni], ex.sin[i0:i0 + ni])
@@ -303,7 +360,11 @@ class Stack:
         gen = torch.Generator(device=device).manual_seed(cfg.seed)
         n = cfg.layers if layers is None else layers
         self.blocks: List[Block] = [Block(cfg, gen, device) for _ in range(n)]
-        cos, sin = rope_tables(cfg, device)
+        # pre-RoPE mode: the current chunk sits at window position cache_chunks
+        # (after the cached chunks, oldest at 0); cached keys are rotated at theirs
+        t_cur = cfg.cache_chunks * cfg.grid[0] if cfg.kv_cache_pre_rope else 0
+        cos, sin = rope_tables(cfg, device, t0=t_cur)
+        self._win_tables = {}
         a, b = self.sp.img_range
         self.cos, self.sin = cos[a:b].contiguous(), sin[a:b].contiguous()
         self.region = None
@@ -320,9 +381,15 @@ class Stack:
             img, txt = blk.forward(img, txt, vec, self.cos, self.sin, kv, self.sp)
         return img, txt
 
+    def window_tables(self, age: int):
+        """fp32 cos/sin of the image grid at window chunk position `age`."""
+        if age not in self._win_tables:
+            self._win_tables[age] = rope_tables(self.cfg, self.device, t0=age * self.cfg.grid[0], fp32=True)
+        return self._win_tables[age]
+
     def commit_kv(self):
         for kv in self.kv:
-            kv.commit(self.sp)
+            kv.commit(self.sp, self.window_tables)
         if self.region is not None and self.sp.world > 1:
             # the next chunk's scatters must not overtake a slower rank's commit copies
             self.region.sync()

@@ -258,6 +258,46 @@ def rope_tables_3d(grid, axes_dims=(44, 42, 42), theta=10000.0):
     return round_bf16(np.concatenate(cs, axis=1)), round_bf16(np.concatenate(ss, axis=1))
 
 
+def rope_apply(x, cos, sin):
+    """RoPE of bf16-valued keys with fp32 tables, the pre-RoPE KV-cache path
+    (deploy/xvideo/models/dit/rope.py:14-28 apply_rotary_emb, called on
+    cached pre-RoPE keys at dit.py:211-217 and at graph commit,
+    deploy/xvideo/serving/graph_runner.py:137-142).
+
+    x: [L, H, D] bf16-valued; cos, sin: [L, D/2] fp32 (the de-duplicated half of
+    the repeat_interleaved tables).  Per pair (x0, x1) = (x[2j], x[2j+1]):
+      rotate_half gives (-x1, x0)                        rope.py:14-18
+      o0 = RN(RN(x0 * c) + RN(-x1 * s))                  rope.py:28, elementwise
+      o1 = RN(RN(x1 * c) + RN( x0 * s))                  torch ops, fp32, no FMA
+    then .type_as(x): bf16 round-to-nearest-even.
+    """
+    x = np.asarray(x, dtype=F32)
+    c = np.asarray(cos, dtype=F32)[:, None, :]
+    s = np.asarray(sin, dtype=F32)[:, None, :]
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    o = np.empty_like(x)
+    o[..., 0::2] = ((x0 * c).astype(F32) + (-x1 * s).astype(F32)).astype(F32)
+    o[..., 1::2] = ((x1 * c).astype(F32) + (x0 * s).astype(F32)).astype(F32)
+    return round_bf16(o)
+
+
+def rope_tables_3d_f32(grid, t0=0, axes_dims=(44, 42, 42), theta=10000.0):
+    """fp32 cos/sin [T*H*W, D/2] for a (t, h, w) grid whose temporal positions
+    start at t0 (the cached-key tables of the pre-RoPE path: get_1d_rotary_pos_embed,
+    rope.py:31-52, over shifted temporal ids, dit.py:955-973), not rounded."""
+    T, H, W = grid
+    tt, hh, ww = np.meshgrid(np.arange(T) + t0, np.arange(H), np.arange(W), indexing="ij")
+    pos = [tt.reshape(-1).astype(F32), hh.reshape(-1).astype(F32), ww.reshape(-1).astype(F32)]
+    cs, ss = [], []
+    for p, d in zip(pos, axes_dims):
+        j = np.arange(0, d, 2, dtype=F32)[: d // 2]
+        f = (F32(1.0) / (F32(theta) ** (j / F32(d)))).astype(F32)
+        ang = np.outer(p, f).astype(F32)
+        cs.append(np.cos(ang).astype(F32))
+        ss.append(np.sin(ang).astype(F32))
+    return np.concatenate(cs, axis=1), np.concatenate(ss, axis=1)
+
+
 # ---------------------------------------------------------------------------
 # K5 FP8 scaled GEMM   (fp8_gemm.cu:834-860 epilogue; fp8_linear.py:100-110 weights)
 # ---------------------------------------------------------------------------

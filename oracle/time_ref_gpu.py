@@ -93,6 +93,7 @@ def main(lib):
         sa = torch.empty((M, 1), dtype=torch.float32, device=dev)
         ops.sgl_per_token_quant_fp8(x, aq, sa)
         for name, NN, gelu in (("cfg3a_fp8_gemm_qkv_bias", 15360, False),
+                               ("cfg3b_fp8_gemm_ffn_up_bias", 13824, False),
                                ("cfg3b_fp8_gemm_ffn_up_bias_then_gelu", 13824, True)):
             wq = (torch.randn(NN, K, generator=gen) * 30).clamp(-448, 448).to(torch.float8_e4m3fn).to(dev).t()
             sb = (torch.rand(NN, generator=gen) * 1e-3).to(dev)

@@ -260,3 +260,20 @@ def test_div448_fma_sequence_exact_for_16bit_inputs():
             q = _rn32(A * F(float(c)))
             r = _rn32(A - F(float(q)) * 448)
             assert _rn32(F(float(r)) * F(float(c)) + F(float(q))) == _rn32(A / 448), a
+
+
+def test_rope_apply_oracle_matches_reference_formula():
+    """O.rope_apply equals apply_rotary_emb of deploy/xvideo/models/dit/rope.py:14-28
+    restated in torch (fp32 elementwise ops, bf16 result), bit for bit."""
+    import torch
+    rng = np.random.default_rng(5)
+    L, H, D = 37, 3, 128
+    x = O.round_bf16(rng.standard_normal((L, H, D)).astype(np.float32) * 3)
+    c, s = O.rope_tables_3d_f32((1, 37, 1), t0=4)
+    xt = torch.from_numpy(x).to(torch.bfloat16)
+    cos = torch.from_numpy(c).repeat_interleave(2, dim=1)[:, None, :]
+    sin = torch.from_numpy(s).repeat_interleave(2, dim=1)[:, None, :]
+    xr, xi = xt.float().reshape(L, H, -1, 2).unbind(-1)
+    rot = torch.stack([-xi, xr], dim=-1).flatten(-2)
+    ref = (xt.float() * cos + rot * sin).to(torch.bfloat16).float().numpy()
+    assert np.array_equal(O.rope_apply(x, c, s), ref)

@@ -76,6 +76,7 @@ def test_ulysses_two_gpus_matches_one(cuda, exchange, port):
                         os.path.join(REPO, "tests", "_stack_mp.py")],
                        capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    print("\n" + "\n".join(ln for ln in r.stdout.splitlines() if ln.startswith("mode")))
     assert "ULYSSES_OK" in r.stdout, r.stdout[-2000:]
 
 

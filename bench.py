@@ -644,11 +644,12 @@ def main():
     ap.add_argument("--e2e-chunks", type=int, default=E2E_CHUNKS, help="row chunks of the end-to-end step")
     ap.add_argument("--only-stack", action="store_true", help="run only the block-stack timing (profiling aid)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    # DRAM bytes (read + write) of one launch of the headline kernel, measured with
-    # ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum on this workload:
-    # 107,897,344 read + 17,900,544 written (part of the 53.9 MB of codes is still
-    # in L2 when the kernel ends, so the write counter undercounts).
-    ap.add_argument("--traffic", type=float, default=107897344 + 17900544,
+    # DRAM bytes (read + write) of one launch of the headline kernel: the mean
+    # over six back-to-back launches on the three rotating sets of
+    # ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum (107.88 MB read,
+    # 14.19 MB written; codes still dirty in L2 at the end of a launch are
+    # written back outside every launch's window, so writes are a lower bound).
+    ap.add_argument("--traffic", type=float, default=107883000 + 14190000,
                     help="DRAM bytes per launch of the headline kernel (ncu)")
     args = ap.parse_args()
     E2E_CHUNKS = max(1, args.e2e_chunks)

@@ -378,6 +378,21 @@ def stack_bench(torch, dev, world):
         blk()
         block_ms[backend] = timed(blk, 5)
     st.cfg.attention = "joyomni"
+    # per-phase breakdown of one block (CUDA events on the stream; max over ranks)
+    breakdown = {}
+    if st.kv[0].peer is not None:
+        st.blocks[0].timer = []
+        blk()
+        torch.cuda.synchronize()
+        marks = st.blocks[0].timer
+        st.blocks[0].timer = None
+        for (_, e0), (name, e1) in zip(marks[:-1], marks[1:]):
+            breakdown[name] = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor(list(breakdown.values()), device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            breakdown = dict(zip(breakdown.keys(), t.tolist()))
+        breakdown = {k: round(v, 3) for k, v in breakdown.items()}
     state = {"x": st.denoise_chunk(x, txt)}          # warm chunk (cache stays full: commit rotates slots)
 
     def chunk():
@@ -401,6 +416,7 @@ def stack_bench(torch, dev, world):
            **({} if graph else {"capture_error": getattr(st, "capture_error", "")}),
            "fps": round(24 / (cms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
            "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
+           "block_breakdown_ms": breakdown,
            "attention": "joyomni_ops.attention (tcgen05 kernel of this repository), bf16",
            "with_torch_sdpa_attention": {"block_ms": round(block_ms["sdpa"], 2),
                                          "chunk_ms": None if chunk_ms["sdpa"] is None else round(chunk_ms["sdpa"], 1),

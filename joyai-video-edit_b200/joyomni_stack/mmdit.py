@@ -264,6 +264,13 @@ class Block:
         self.cfg = cfg
         self.img = Stream(cfg, gen, device)
         self.txt = Stream(cfg, gen, device)
+        self.timer = None       # a list: CUDA events at phase boundaries (bench breakdown)
+
+    def _mark(self, name: str):
+        if self.timer is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.timer.append((name, ev))
 
     def forward(self, img, txt, vec, cos, sin, kv: LayerKV, sp: SeqParallel):
         cfg = self.cfg
@@ -311,12 +318,15 @@ class Block:
         Dh, D = cfg.head_dim, cfg.hidden
         Li = img.shape[0]
         ex = kv.peer
+        self._mark("start")
         xq, xs = norm_mod_quant(img, im[0], im[1])
         self.img.qkv.scatter(xq, xs, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0], ex.q.shape[0])
         tq, ts = norm_mod_quant(txt, tm[0], tm[1])
         self.txt.qkv.scatter(tq, ts, ex.dst, sp.world, sp.local_heads, Dh, ex.seg[sp.rank][0] + Li, ex.q.shape[0])
+        self._mark("norm_quant_qkv_scatter_gemm")
         if ex.region is not None:
             ex.region.sync()
+        self._mark("exchange_sync")
         q = ex.q
         if kv.keep_q:
             kv.last_k_raw = kv.k[:kv.cur].clone()
@@ -334,10 +344,15 @@ class Block:
                                         NORM_EPS, self.txt.q_norm, self.txt.k_norm)
         if kv.keep_q:
             kv.last_q = q.clone()
+        self._mark("qk_norm_rope")
         k_all, v_all = kv.keys()
-        o = sp.heads_to_seq(attend(q, k_all, v_all, self.cfg.attention)).reshape(Li + txt.shape[0], D)
+        o = attend(q, k_all, v_all, self.cfg.attention)
+        self._mark("attention")
+        o = sp.heads_to_seq(o).reshape(Li + txt.shape[0], D)
+        self._mark("output_all_to_all")
         img = self._tail(self.img, im, img, o[:Li])
         txt = self._tail(self.txt, tm, txt, o[Li:])
+        self._mark("proj_ffn_gemms")
         return img, txt
 
     @staticmethod

@@ -624,6 +624,15 @@ static StagedGeom pick_geom(int nvec, int op, int norm) {
     if (staged::is_modrow(op)) return StagedGeom{5, 2, 2};
     return StagedGeom{5, 1, 2};
   }
+  // N = 4096, the shipped model's hidden size (deploy/xvideo/config.py:22): the
+  // same team shapes scaled to 512 vectors (2-warp teams of 8 for rms, 4-warp
+  // teams of 4 otherwise).
+  if (nvec == 512) {
+    if ((op == staged::OP_NORM_MOD_QUANT || op == staged::OP_NORM_MOD) && norm == JO_NORM_RMS)
+      return StagedGeom{8, 1, 2};
+    if (staged::is_modrow(op)) return StagedGeom{4, 2, 2};
+    return StagedGeom{4, 1, 2};
+  }
   return StagedGeom{4, 2, 2};
 }
 
@@ -637,7 +646,7 @@ static bool fixed_enabled() {
   return v == 1;
 }
 
-#define N_FIXED_OK(g, nvec) ((nvec) == 640)
+#define N_FIXED_OK(g, nvec) ((nvec) == 640 || (nvec) == 512)
 template <typename T, int OP, int NORM>
 static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream_t st) {
   using namespace staged;
@@ -647,12 +656,14 @@ static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream
     // One row of x, scale and shift per slot, two slots per team.
     if (fixed_enabled() && g.vpl == 5 && nvec == 640) return launch<T, OP, NORM, 5, 2, 1, 4>(a, team, st);
     if (fixed_enabled() && g.vpl == 4 && nvec == 640) return launch<T, OP, NORM, 4, 2, 1, 5>(a, team, st);
+    if (fixed_enabled() && g.vpl == 4 && nvec == 512) return launch<T, OP, NORM, 4, 2, 1, 4>(a, team, st);
     return launch<T, OP, NORM, 4, 2, 1, 0>(a, ((nvec + 3) / 4 + 31) / 32 * 32, st);
   } else {
-  // Fixed geometries for the model's widths: N = 5120 (hidden) and 3072.
+  // Fixed geometries for the model's widths: N = 5120 (hidden), 4096 and 3072.
   if (g.vpl == 4 && g.r == 2 && g.s == 2 && team * 4 == nvec && fixed_enabled()) {
     if (team == 160) return launch<T, OP, NORM, 4, 2, 2, 5>(a, team, st);
     if (team == 96) return launch<T, OP, NORM, 4, 2, 2, 3>(a, team, st);
+    if (team == 128) return launch<T, OP, NORM, 4, 2, 2, 4>(a, team, st);
   }
   if (fixed_enabled() && N_FIXED_OK(g, nvec)) {
 #define JO_F(V, R, S, W) \
@@ -660,6 +671,8 @@ static int launch_geom(const staged::Args& a, int nvec, StagedGeom g, cudaStream
     JO_F(5, 1, 2, 4)
     JO_F(5, 2, 2, 4)
     JO_F(10, 1, 2, 2)
+    JO_F(8, 1, 2, 2)
+    JO_F(4, 1, 2, 4)
 #undef JO_F
   }
 #define JO_G(V, R, S) \

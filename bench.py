@@ -526,7 +526,8 @@ def gemm_table(torch, jo, dev, gen):
     aq = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=dev)
     sa = torch.empty(M, dtype=torch.float32, device=dev)
     jo.sgl_per_token_quant_fp8(a, aq, sa)
-    for name, N, gelu in (("cfg3a_fp8_gemm_qkv_bias", 15360, False), ("cfg3b_fp8_gemm_ffn_up_bias_gelu", 13824, True)):
+    for name, N, gelu in (("cfg3a_fp8_gemm_qkv_bias", 15360, False), ("cfg3b_fp8_gemm_ffn_up_bias", 13824, False),
+                          ("cfg3b_fp8_gemm_ffn_up_bias_gelu", 13824, True)):
         wq = (torch.randn(N, K, generator=gen) * 30).clamp(-448, 448).to(torch.float8_e4m3fn).to(dev).t()
         sb = (torch.rand(N, generator=gen) * 1e-3).to(dev)
         bias = (0.01 * torch.randn(N, generator=gen)).to(torch.bfloat16).to(dev)

@@ -140,12 +140,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// GELU, tanh form: 0.5 * y * (1 + tanh(u)) with u = sqrt(2/pi) * (y + 0.044715 y^3)
+// (F.gelu(approximate="tanh") as the reference model applies it, dit.py:90-92),
+// evaluated through the identity 0.5 * (1 + tanh(u)) = 1 / (1 + 2^(-2 u log2 e)):
+// one SFU exponential and one SFU reciprocal, each accurate to about 2^-22
+// relative, and no cancellation for negative y (where 1 + tanh(u) is small and
+// an approximate tanh would lose most of its digits).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 __device__ __forceinline__ float gelu_tanh(float y) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float u = k0 * (y + 0.044715f * y * y * y);
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
-  return 0.5f * y * (1.f + t);
+  const float k_beta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k_kappa = 0.044715f;
+  const float k_m2log2e = -2.8853900817779268f;  // -2 log2(e)
+  const float u = k_beta * (y + k_kappa * (y * y * y));
+  return y * rcp_approx(1.f + ex2_approx(k_m2log2e * u));
 }
 
 struct Params {

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import joyomni_oracle as O
-from _util import assert_close_ulp, randn
+from _util import assert_close_ulp, randn, rel_rms, ulp
 
 pytestmark = pytest.mark.gpu
 
@@ -19,6 +19,18 @@ def jo(cuda):
     if not joyomni_ops.has_fp8():
         pytest.skip("GEMM not built")
     return joyomni_ops
+
+
+def assert_close_gelu(got, ref, pre):
+    """GELU of a GEMM output: within 2 ulps of the output plus the GELU of a
+    1-ulp change of its input (|gelu'| <= 1.13), since the GEMM output itself
+    may sit one rounding away from the oracle's (fp32 accumulation order) and
+    GELU's slope carries that into outputs much smaller than their inputs."""
+    got, ref, pre = (np.asarray(t, dtype=np.float64) for t in (got, ref, pre))
+    tol = 2 * ulp(np.maximum(np.abs(got), np.abs(ref))) + 1.13 * ulp(np.abs(pre)) + 1e-6
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} beyond tolerance; worst {np.abs(got - ref)[bad].max():.3e}"
+    assert rel_rms(got, ref) <= 2e-3
 
 
 def _operands(rng, M, N, K):
@@ -60,7 +72,7 @@ def test_fp8_scaled_mm_gelu(jo, cuda, M, N, K):
     bias = randn(rng, (N,), 0.5)
     y = _run(jo, cuda, a, sa, b, sb, bias, gelu=True)
     ref = O.fp8_scaled_mm(a, b, sa, sb, bias, epilogue="gelu_tanh")
-    assert_close_ulp(y.float().cpu().numpy(), ref, max_ulp=2, rel_rms=2e-3, atol=1e-4)
+    assert_close_gelu(y.float().cpu().numpy(), ref, O.fp8_scaled_mm(a, b, sa, sb, bias))
 
 
 def test_fp8_scaled_mm_fp16_out(jo, cuda):
@@ -101,7 +113,10 @@ def test_fp8_scaled_mm_full_size_row_sample(jo, cuda, N, gelu):
     y = _run(jo, cuda, a, sa, b, sb, bias, gelu=gelu).float().cpu().numpy()
     rows = np.unique(np.concatenate([np.random.default_rng(2).integers(0, M, 24), [0, 127, 128, M - 35, M - 1]]))
     ref = O.fp8_scaled_mm(a[rows], b, sa[rows], sb, bias, epilogue="gelu_tanh" if gelu else "none")
-    assert_close_ulp(y[rows], ref, max_ulp=2, rel_rms=2e-3 if gelu else 1e-3, atol=1e-4 if gelu else 1e-6)
+    if gelu:
+        assert_close_gelu(y[rows], ref, O.fp8_scaled_mm(a[rows], b, sa[rows], sb, bias))
+    else:
+        assert_close_ulp(y[rows], ref, max_ulp=2, rel_rms=1e-3)
     assert np.isfinite(y).all()
 
 
@@ -184,13 +199,15 @@ def test_fp8_scaled_mm_scatter_rejects_bad_layout(jo, cuda):
 
 
 def test_gelu_epilogue_error_bound_full_cfg3b(jo, cuda):
-    """The GELU-tanh epilogue evaluates tanh with tanh.approx.f32 (maximum
-    relative error 2^-10.99 per the PTX ISA), where the reference model calls
-    F.gelu(approximate="tanh") on the bf16 GEMM output (dit.py:90-92).  Over the
-    whole config-3b output (10530 x 13824) the fused result must stay within
-    1 bf16 ulp (plus 1e-6 absolute near zero) of F.gelu applied in fp32 to this
-    repository's plain GEMM output (the same accumulator), which isolates the
-    epilogue; the fraction of elements that differ is reported."""
+    """The GELU-tanh epilogue applies GELU to the bf16-rounded GEMM output in
+    fp32, as the reference model calls F.gelu(approximate="tanh") on the bf16
+    GEMM output (dit.py:90-92).  Over the whole config-3b output (10530 x 13824)
+    the fused result must stay within 1 bf16 ulp (plus 1e-6 absolute near zero)
+    of F.gelu applied in fp32 to this repository's plain GEMM output (the same
+    accumulator), which isolates the epilogue; the fraction of elements that
+    differ is reported.  (tanh.approx.f32 in place of the exponential form
+    measured 1.48 ulp here: it loses 1 + tanh(u) of negative inputs to
+    cancellation.)"""
     import torch.nn.functional as F
     M, N, K = 10530, 13824, 5120
     g = torch.Generator(device="cpu").manual_seed(7)

@@ -15,15 +15,17 @@
 // UMMA K-major SW128 layout.  No cluster multicast anywhere: every CTA loads its
 // own tiles; operand reuse across CTAs comes from L2 via a grouped tile order.
 //
-// Kernel organisation (one persistent CTA per SM, 192 threads):
+// Kernel organisation (one persistent CTA per SM, 320 threads):
 //   warp 0      TMA producer: K-blocks of 128 bytes for A (128 rows) and B (256 rows)
 //               into a ring of STAGES shared-memory stages (full/empty mbarriers)
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (K = 32)
 //               per stage into one of two 128 x 256 fp32 accumulators in TMEM
 //               (512 columns), tcgen05.commit releases the stage / publishes the tile
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, scales + bias (+ GELU),
-//               bf16/fp16 stores; the accumulator is handed back so the MMA of the
-//               next tile overlaps this epilogue.
+//   warps 2..9  epilogue, two warps per TMEM lane quarter, each draining half of
+//               the columns: tcgen05.ld 32 columns at a time (the next chunk's load
+//               in flight), scales + bias (+ GELU), bf16/fp16 stores; the
+//               accumulator is handed back so the MMA of the next tile overlaps
+//               this epilogue.
 // Every mbarrier wait is bounded by a clock-based timeout; on expiry the CTA sets
 // an abort flag, records an error code readable with jo_gemm_last_fault(), waits
 // (bounded) for its own in-flight copies, frees its TMEM and returns.
@@ -42,7 +44,8 @@ constexpr int STAGES = 4;
 constexpr int A_STAGE = BM * BK;              // 16 KB
 constexpr int B_STAGE = BN * BK;              // 32 KB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;            // producer, MMA issuer, 8 epilogue warps
+constexpr int EPI_WARPS = 8;
 constexpr int TMEM_COLS = 512;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -262,6 +265,30 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], const Pa
   }
 }
 
+// One epilogue warp's share of an accumulator tile: the 32 rows of its TMEM
+// lane quarter, columns [128 half, 128 half + 128) of the BN columns, in four
+// 32-column chunks; the TMEM load of the next chunk is in flight while the
+// current one is converted and stored.  Eight warps (two per lane quarter)
+// drain a tile in about half the time four would.
+template <typename OutT>
+__device__ __forceinline__ void drain_tile(const Params& p, uint32_t tbase, int m, bool mok, float sa, int nb,
+                                           int half) {
+  OutT* drow = static_cast<OutT*>(p.d) + (size_t)(mok ? m : 0) * p.N;
+  constexpr int CH = BN / 2 / 32;
+  const uint32_t t0 = tbase + half * (BN / 2);
+  uint32_t r[2][32];
+  __syncwarp();
+  tmem_ld32(t0, r[0]);
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    tmem_wait_ld();  // chunk i has landed (nothing else is outstanding)
+    if (i + 1 < CH) tmem_ld32(t0 + (i + 1) * 32, r[(i + 1) & 1]);
+    const int n0 = nb * BN + half * (BN / 2) + i * 32;
+    if (mok && n0 < p.N)
+      epilogue_chunk<OutT>(r[i & 1], p, m, sa, n0, p.scatter ? scatter_dst<OutT>(p, m, n0) : drow + n0);
+  }
+}
+
 // Grouped rasterisation: GROUP m-blocks share the n sweep, keeping the live
 // A and B panels of all 148 CTAs inside L2.
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
@@ -301,7 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 4);
+      mbar_init(tempty0 + 8 * b, EPI_WARPS);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -386,9 +413,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ------------------------------------------------------------- epilogue --
     const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;      // column half of the tile
     const int row_in_tile = quarter * 32 + lane;
     int tc = 0;
-    OutT* D = static_cast<OutT*>(p.d);
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
       int mb, nb;
       tile_coords(t, p, mb, nb);
@@ -399,18 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int m = mb * BM + row_in_tile;
       const bool mok = m < p.M;
       const float sa = mok ? __ldg(p.sa + m) : 0.f;
-      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
-      OutT* drow = D + (size_t)(mok ? m : 0) * p.N;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(tbase + c, r);
-        tmem_wait_ld();
-        const int n0 = nb * BN + c;
-        if (!mok || n0 >= p.N) continue;
-        epilogue_chunk<OutT>(r, p, m, sa, n0, p.scatter ? scatter_dst<OutT>(p, m, n0) : drow + n0);
-      }
+      drain_tile<OutT>(p, tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN, m, mok, sa, nb, half);
       // hand the accumulator back to the MMA warp
       fence_before();
       __syncwarp();
@@ -550,7 +566,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);   // one multicast commit per tile
-      mbar_init(tempty0 + 8 * b, 8);  // leader only: 4 epilogue warps x 2 CTAs
+      mbar_init(tempty0 + 8 * b, 2 * EPI_WARPS);  // leader only: epilogue warps of both CTAs
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -634,10 +650,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else {
     // ------------------------------------------------------------- epilogue --
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t ltempty0 = map_to_rank(tempty0, 0);
     int tc = 0;
-    OutT* D = static_cast<OutT*>(p.d);
     for (int t = pair; t < num_tiles; t += npairs, ++tc) {
       int mb, nb;
       tile_coords2(t, p.m_blocks, p.n_blocks, p.group, mb, nb);
@@ -648,18 +664,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int m = mb * 256 + (int)rank * 128 + row_in_tile;
       const bool mok = m < p.M;
       const float sa = mok ? __ldg(p.sa + m) : 0.f;
-      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
-      OutT* drow = D + (size_t)(mok ? m : 0) * p.N;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(tbase + c, r);
-        tmem_wait_ld();
-        const int n0 = nb * BN + c;
-        if (!mok || n0 >= p.N) continue;
-        epilogue_chunk<OutT>(r, p, m, sa, n0, p.scatter ? scatter_dst<OutT>(p, m, n0) : drow + n0);
-      }
+      drain_tile<OutT>(p, tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN, m, mok, sa, nb, half);
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(ltempty0 + 8 * buf);

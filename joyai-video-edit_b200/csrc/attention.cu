@@ -166,6 +166,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// max of three floats in one instruction (NaN operands are ignored).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -354,9 +360,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= last_valid) s[i] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max as four independent chains of three-input max (depth 17
+      // instead of a 127-long dependent chain).
+      float mq[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 4; i < 124; i += 8)
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) mq[q4] = max3f(mq[q4], s[i + 2 * q4], s[i + 2 * q4 + 1]);
+      mq[0] = max3f(mq[0], s[124], s[125]);
+      mq[1] = max3f(mq[1], s[126], s[127]);
+      const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
       const float mt = mx * c;
       // Raise the running max only when the tile's max exceeds it by 2^8 (or on
       // the first tile); otherwise p <= 2^8 stays well inside fp32 / bf16 range.
@@ -366,12 +379,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float alpha = ex2(m - m_new);  // 1 when the max is kept; 0 on the first tile
       m = m_new;
       const float mneg = -m;
-      float rs = 0.f;
+      // p = 2^(s*c - m): the argument two lanes per instruction, the row sum
+      // in four independent paired accumulators.
+      const float2 c2 = make_float2(c, c), mn2 = make_float2(mneg, mneg);
+      float2 ra[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        s[i] = ex2(__fmaf_rn(s[i], c, mneg));
-        rs += s[i];
+      for (int i = 0; i < 128; i += 2) {
+        float2 e = fma2(make_float2(s[i], s[i + 1]), c2, mn2);
+        e.x = ex2(e.x);
+        e.y = ex2(e.y);
+        s[i] = e.x;
+        s[i + 1] = e.y;
+        ra[(i >> 1) & 3] = add2(ra[(i >> 1) & 3], e);
       }
+      const float2 r01 = add2(ra[0], ra[1]), r23 = add2(ra[2], ra[3]);
+      const float rs = (r01.x + r01.y) + (r23.x + r23.y);
       l = __fmaf_rn(l, alpha, rs);
       {
         uint32_t pk[64];

@@ -348,6 +348,12 @@ class Block:
         k_all, v_all = kv.keys()
         o = attend(q, k_all, v_all, self.cfg.attention)
         self._mark("attention")
+        # Every layer shares the one head-sharded q buffer in the peer region:
+        # a faster rank's next-layer scatter may only start once this rank's
+        # attention has finished reading q.  heads_to_seq is an NCCL all-to-all
+        # that no rank leaves before every rank has entered it (after its
+        # attention), which gives that ordering; an asynchronous or peer-based
+        # output exchange would need an explicit region.sync() here instead.
         o = sp.heads_to_seq(o).reshape(Li + txt.shape[0], D)
         self._mark("output_all_to_all")
         img = self._tail(self.img, im, img, o[:Li])

@@ -303,15 +303,20 @@ def rope_tables_3d_f32(grid, t0=0, axes_dims=(44, 42, 42), theta=10000.0):
 # ---------------------------------------------------------------------------
 
 
-def quantize_weight_per_channel(w):
+def quantize_weight_per_channel(w, on_cuda=False):
     """w: [N, K] bf16-valued -> (codes [N, K] uint8 (= column-major [K, N]), scale f32 [N]).
 
     scale = max(absmax_k |W[n,:]|, 1e-8) / 448 ; q = e4m3(clamp(W / scale, +-448))
     (deploy/xvideo/models/dit/fp8_linear.py:100-110; fp32 division).
+
+    on_cuda=True follows the same torch code run on a GPU: ATen's CUDA true
+    division by a Python scalar multiplies by the scalar's fp32 reciprocal, so
+    the scale there is RN(absmax * RN(1/448)) (up to one ulp away from the
+    quotient); the division of W by the scale tensor stays an IEEE division.
     """
     w = np.asarray(w, dtype=F32)
     amax = np.maximum(np.abs(w).max(axis=1), F32(1e-8)).astype(F32)
-    s = (amax / FP8_MAX).astype(F32)
+    s = (amax * (F32(1.0) / FP8_MAX)).astype(F32) if on_cuda else (amax / FP8_MAX).astype(F32)
     v = (w / s[:, None]).astype(F32)
     v = np.clip(v, -FP8_MAX, FP8_MAX)
     return e4m3_encode(v), s

@@ -135,45 +135,45 @@ __device__ __forceinline__ void team_umax(uint32_t (&v)[R], int team, int bar_id
                  [](uint32_t x, uint32_t y) { return max(x, y); });
 }
 
-// Row statistics on the tensor cores, m16n8k8 with fp32 accumulation.  Per
-// thread the A fragment is one register pair (row g = lane/4 and row g + 8 of
-// A, two 16-bit elements each) and B one register (column g).  With A = {u, v}
-// (two words of ONE row, as loaded: no register moves) and B = u, the
-// diagonal D[g][g] gains the squares of u over the four threads of group g
-// (rows g + 8 gain cross products u*v, unused); with B = v, D[g+8][g] gains
-// the squares of v (rows g gain cross products).  The two forms therefore
-// accumulate in separate registers.  With B = ones, every D[g][n] gains the
-// plain sum of u of group g and D[g+8][n] that of v.  The products are exact
-// in fp32 (16-bit inputs); only the accumulation order differs from a scalar
-// loop.
+// Row statistics on the tensor cores, m16n8k16 with fp32 accumulation, on
+// the registers as loaded: the squares of the words that sit in A rows g land
+// on the diagonal D[g][g], those in rows g + 8 on D[g+8][g] (the other
+// products are unused cross terms), so the two forms accumulate in separate
+// registers; with B = ones every D[g][n] gains the plain sum of rows g.  The
+// products are exact in fp32 (16-bit inputs); only the accumulation order
+// differs from a scalar loop.
 template <typename T> struct MmaType;
 template <> struct MmaType<__nv_bfloat16> { static constexpr uint32_t kOnes = 0x3f803f80u; };
 template <> struct MmaType<__half> { static constexpr uint32_t kOnes = 0x3c003c00u; };
+// m16n8k16: A fragment {a0, a1, a2, a3} = (row g, k 0-1), (row g + 8, k 0-1),
+// (row g, k 8-9), (row g + 8, k 8-9) of this thread's group; B {b0, b1} =
+// (k 0-1, column g), (k 8-9, column g).  With A = {x, y, z, w} (the four words
+// of one loaded vector, no moves) and B = {x, z}, D[g][g] gains x.x + z.z over
+// the group; with B = {y, w}, D[g + 8][g] gains y.y + w.w.
 template <typename T>
-__device__ __forceinline__ void mma_k8(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b) {
+__device__ __forceinline__ void mma_k16(float (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value)
-    asm("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(b));
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
   else
-    asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(b));
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 // Sum of squares of one 16-byte vector: words x, z into the top diagonal of
-// cu, words y, w into the bottom diagonal of cv.
+// cu, words y, w into the bottom diagonal of cv (two instructions per vector).
 template <typename T>
 __device__ __forceinline__ void mma_sumsq(float (&cu)[4], float (&cv)[4], const uint4& v) {
-  mma_k8<T>(cu, v.x, v.y, v.x);
-  mma_k8<T>(cv, v.x, v.y, v.y);
-  mma_k8<T>(cu, v.z, v.w, v.z);
-  mma_k8<T>(cv, v.z, v.w, v.w);
+  mma_k16<T>(cu, v, v.x, v.z);
+  mma_k16<T>(cv, v, v.y, v.w);
 }
 // Plain sum of one 16-byte vector into c (column 0 of rows g and g + 8).
 template <typename T>
 __device__ __forceinline__ void mma_sum(float (&c)[4], const uint4& v) {
-  mma_k8<T>(c, v.x, v.y, MmaType<T>::kOnes);
-  mma_k8<T>(c, v.z, v.w, MmaType<T>::kOnes);
+  mma_k16<T>(c, v, MmaType<T>::kOnes, MmaType<T>::kOnes);
 }
 // This lane's share of the squares: D[g][g] of cu plus D[g+8][g] of cv; of
 // the plain sums: D[g][0] + D[g+8][0]; zero on the other lanes.

@@ -399,11 +399,17 @@ def stack_bench(torch, dev, world):
         state["x"] = st.denoise_chunk(state["x"], txt)
     chunk_ms_eager = timed(chunk, 1)
     chunk_ms, graphs = {}, {}
+    store_ms = None
     for backend in ("joyomni", "sdpa"):
         st.cfg.attention = backend
         graphs[backend] = st.capture(txt)             # whole 40-layer step in one CUDA graph
         chunk()
         chunk_ms[backend] = timed(chunk, 1) if graphs[backend] else (chunk_ms_eager if backend == "joyomni" else None)
+        if backend == "joyomni":
+            # with the reference's extra store forward on the clean latent
+            def chunk_store():
+                state["x"] = st.denoise_chunk(state["x"], txt, store_pass=True)
+            store_ms = timed(chunk_store, 1)
     st.cfg.attention = "joyomni"
     graph = graphs["joyomni"]
     finite = bool(torch.isfinite(state["x"]).all())
@@ -415,6 +421,9 @@ def stack_bench(torch, dev, world):
            "chunk_ms_eager": round(chunk_ms_eager, 1), "step_cuda_graph": graph,
            **({} if graph else {"capture_error": getattr(st, "capture_error", "")}),
            "fps": round(24 / (cms / 1e3), 2), "frames_per_chunk": 24, "target_fps": 30,
+           "with_store_pass": {"chunk_ms": round(store_ms, 1), "fps": round(24 / (store_ms / 1e3), 2),
+                               "what": "plus the reference's store forward on the clean latent (run as a full "
+                                       "step: an upper bound, the reference skips the text stream there)"},
            "block_tflop": round((gflop_block + attn_flop) / 1e3, 2), "finite": finite,
            "block_breakdown_ms": breakdown,
            "attention": "joyomni_ops.attention (tcgen05 kernel of this repository), bf16",

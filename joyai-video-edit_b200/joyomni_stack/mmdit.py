@@ -19,8 +19,9 @@ random-initialised weights and synthetic inputs.  Per block and stream:
 Differences from the reference model that the synthetic configuration asks
 for or that are harness simplifications: BASELINE's dims (hidden 5120, 40
 heads, FFN 13824, RoPE split 44/42/42); the KV cache stores post-RoPE keys of
-the image tokens of the last 2 chunks, written from the last denoising step
-(no separate clean-latent store forward); the latent <-> token projections and
+the image tokens of the last 2 chunks (or pre-RoPE keys, kv_cache_pre_rope),
+written from the last denoising step, or with store_pass=True from an extra
+forward on the clean latent as the reference does; the latent <-> token projections and
 the Euler update act directly in token space.  Sequence parallelism (Ulysses,
 ulysses.py) is new; with P = 1 it degenerates to plain single-GPU execution.
 """
@@ -536,14 +537,23 @@ class Stack:
         g.replay()
         return self._gout
 
-    def denoise_chunk(self, x: torch.Tensor, txt: torch.Tensor, timesteps=(1000, 750, 500)):
+    def denoise_chunk(self, x: torch.Tensor, txt: torch.Tensor, timesteps=(1000, 750, 500),
+                      store_pass: bool = False):
         """3 denoising steps (Euler in fp32 over sigmas t/1000 -> next, last -> 0);
         the chunk's image K/V from the last step enter the cache afterwards.  Uses
-        the captured step graph when capture() succeeded."""
+        the captured step graph when capture() succeeded.
+
+        store_pass=True adds the reference's extra forward on the clean latent at
+        timestep 0 whose K/V are the ones cached (pipeline.py:411-448,
+        graph_runner.py:156-163).  The reference skips the text stream in that
+        pass (skip_text_stream=True, pipeline.py:447); here it runs the same full
+        step (graph), so its cost is an upper bound by the text tokens' share."""
         sig = [t / 1000.0 for t in timesteps] + [0.0]
         for i, t in enumerate(timesteps):
             v = self._step(x.to(torch.bfloat16), txt, self.timestep_vec(t))
             x = x + (sig[i + 1] - sig[i]) * v.float()
+        if store_pass:
+            self._step(x.to(torch.bfloat16), txt, self.timestep_vec(0))
         self.commit_kv()
         jo.check_gemm_fault(self.device)     # a GEMM that gave up on a wait returned partial output
         return x

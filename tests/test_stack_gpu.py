@@ -63,6 +63,33 @@ def test_kv_cache_ring(cuda):
     assert torch.isfinite(x).all()
 
 
+def test_store_pass_caches_clean_latent_kv(cuda):
+    """denoise_chunk(store_pass=True) caches the V of a forward on the returned
+    (clean) latent at timestep 0 (the reference's store forward,
+    pipeline.py:411-448), not that of the last denoising step.  With one layer
+    V depends only on the chunk's own tokens, so it can be recomputed exactly."""
+    from joyomni_stack import Stack
+    cfg = _small_cfg(layers=1)
+    st = Stack(cfg, cuda)
+    x, txt = st.inputs(5)
+    kv = st.kv[0]
+    (start, length), = st.sp.gathered_img_segments()
+    slot = kv.next_slot
+    x1 = st.denoise_chunk(x, txt, store_pass=True)
+    base = kv.cur + slot * cfg.img_tokens
+    cached = kv.v[base:base + length].clone()
+    st.forward(x1.to(torch.bfloat16), txt, st.timestep_vec(0))
+    assert torch.equal(cached, kv.v[start:start + length])
+    # without the store pass the slot holds the last denoising step's V instead
+    st2 = Stack(cfg, cuda)
+    slot2 = st2.kv[0].next_slot
+    st2.denoise_chunk(x, txt)
+    b2 = st2.kv[0].cur + slot2 * cfg.img_tokens
+    last_step_v = st2.kv[0].v[b2:b2 + length]
+    assert not torch.equal(cached, last_step_v)
+    assert torch.isfinite(x1).all()
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("exchange,port", [("peer", 29517), ("nccl", 29518)])
 def test_ulysses_two_gpus_matches_one(cuda, exchange, port):

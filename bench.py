@@ -297,6 +297,10 @@ def run_ours(args):
         if world == 1:
             ref_gpu = reference_gpu_table()
             cpu = cpu_baseline(args.cpu_seconds)
+            try:
+                cpu["other_configs"] = cpu_other_configs(cpu["cores"])
+            except Exception as e:  # noqa: BLE001  (host memory etc.: the headline baseline stands)
+                cpu["other_configs"] = {"error": repr(e)[:200]}
     pk = peaks()
     if rank == 0:
         achieved = bytes_step / (avg_launch_us * 1e-6) / 1e9
@@ -627,6 +631,42 @@ def cpu_baseline(seconds):
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{reps} passes over {rows} of {M_CFG2} rows of cfg2, eager-torch fp32 restatement of the "
                       f"reference (norm_scale_shift RMS then per-token quant), {threads} threads, {dt:.1f} s"}
+
+
+def cpu_other_configs(threads):
+    """Configs 1 and 3a through the reference's eager-torch math
+    (oracle/torch_eager.py) at full size on the host cores: one warm and one
+    timed run each."""
+    import torch
+
+    import torch_eager
+    torch.set_num_threads(threads)
+    g = torch.Generator(device="cpu").manual_seed(11)
+    out = {}
+    L, H, D = 2048, 40, 128
+    q = torch.randn(L * H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(L * H, D, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    cs = torch.rand(L, D // 2, generator=g).to(torch.bfloat16)
+    torch_eager.cfg1_qk_norm_rope(q, k, w, w, cs, cs, H)
+    t0 = time.perf_counter()
+    torch_eager.cfg1_qk_norm_rope(q, k, w, w, cs, cs, H)
+    dt = time.perf_counter() - t0
+    by = 4 * L * H * D * 2 + 2 * L * (D // 2) * 2
+    out["cfg1_qk_norm_rope"] = {"ms": round(dt * 1e3, 2), "GB/s": round(by / dt / 1e9, 3)}
+    M, K, N = M_CFG2, N_CFG2, 15360
+    a = (torch.randn(M, K, generator=g) * 30).clamp(-448, 448).to(torch.float8_e4m3fn)
+    b = (torch.randn(N, K, generator=g) * 30).clamp(-448, 448).to(torch.float8_e4m3fn)
+    sa, sb = torch.rand(M, generator=g) * 1e-3, torch.rand(N, generator=g) * 1e-3
+    bias = (0.01 * torch.randn(N, generator=g)).to(torch.bfloat16)
+    torch_eager.cfg3_fp8_scaled_mm(a[:512], b, sa[:512], sb, bias)
+    t0 = time.perf_counter()
+    torch_eager.cfg3_fp8_scaled_mm(a, b, sa, sb, bias)
+    dt = time.perf_counter() - t0
+    out["cfg3a_fp8_gemm_qkv_bias"] = {"ms": round(dt * 1e3, 1), "TFLOP/s": round(2 * M * N * K / dt / 1e12, 3)}
+    out["what"] = (f"eager-torch fp32 restatement of the reference math, full size, {threads} threads "
+                   "(fp8 operands dequantised to fp32 for the GEMM)")
+    return out
 
 
 def run_reference(args):

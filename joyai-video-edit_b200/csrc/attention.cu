@@ -163,6 +163,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 #undef JO_W8
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -383,25 +391,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       // in four independent paired accumulators.
       const float2 c2 = make_float2(c, c), mn2 = make_float2(mneg, mneg);
       float2 ra[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      // P goes to tensor memory in four chunks of 32 keys as soon as each is
+      // done, so the stores overlap the exponentials of the next chunk.
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        float2 e = fma2(make_float2(s[i], s[i + 1]), c2, mn2);
-        e.x = ex2(e.x);
-        e.y = ex2(e.y);
-        s[i] = e.x;
-        s[i + 1] = e.y;
-        ra[(i >> 1) & 3] = add2(ra[(i >> 1) & 3], e);
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 32 * ch; i < 32 * ch + 32; i += 2) {
+          float2 e = fma2(make_float2(s[i], s[i + 1]), c2, mn2);
+          e.x = ex2(e.x);
+          e.y = ex2(e.y);
+          pk[(i - 32 * ch) >> 1] = pack2<__nv_bfloat16>(e.x, e.y);
+          ra[(i >> 1) & 3] = add2(ra[(i >> 1) & 3], e);
+        }
+        tmem_st16(tS + 16 * ch, pk);
       }
       const float2 r01 = add2(ra[0], ra[1]), r23 = add2(ra[2], ra[3]);
       const float rs = (r01.x + r01.y) + (r23.x + r23.y);
       l = __fmaf_rn(l, alpha, rs);
-      {
-        uint32_t pk[64];
-#pragma unroll
-        for (int i = 0; i < 64; ++i) pk[i] = pack2<__nv_bfloat16>(s[2 * i], s[2 * i + 1]);
-        tmem_st32(tS, pk);
-        tmem_st32(tS + 32, pk + 32);
-      }
       // O_t *= alpha, in tensor memory (PV_t of the previous tile has completed:
       // it was issued before the QK_t whose completion released this S tile).
       if (any_need && j > 0) {

@@ -636,7 +636,7 @@ def cpu_baseline(seconds):
 def cpu_other_configs(threads):
     """Configs 1 and 3a through the reference's eager-torch math
     (oracle/torch_eager.py) at full size on the host cores: one warm and one
-    timed run each."""
+    timed run each; config 4 (and 5, extrapolated) through cpu_block."""
     import torch
 
     import torch_eager
@@ -664,9 +664,49 @@ def cpu_other_configs(threads):
     torch_eager.cfg3_fp8_scaled_mm(a, b, sa, sb, bias)
     dt = time.perf_counter() - t0
     out["cfg3a_fp8_gemm_qkv_bias"] = {"ms": round(dt * 1e3, 1), "TFLOP/s": round(2 * M * N * K / dt / 1e12, 3)}
+    if os.environ.get("JO_CPU_BLOCK", "1") != "0":
+        out["cfg4_block"] = cpu_block(threads)
     out["what"] = (f"eager-torch fp32 restatement of the reference math, full size, {threads} threads "
-                   "(fp8 operands dequantised to fp32 for the GEMM)")
+                   "(fp8 operands dequantised to fp32 for the GEMMs)")
     return out
+
+
+def cpu_block(threads):
+    """Config 4 on the host cores: one MMDiT block (10530 image + 512 text
+    tokens, 40 heads, KV cache of 2 x 10530 image tokens) through the eager-torch
+    restatement (oracle/torch_eager.py:cfg4_block), random FP8 weights of the
+    model's shapes, timed once; config 5 reported as 120 blocks (40 layers x 3
+    steps), extrapolated.  About 12.7 TFLOP, tens of seconds."""
+    import torch
+
+    import torch_eager
+    torch.set_num_threads(threads)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    D, H, Dh, Fh, Li, Lt, Lc = 5120, 40, 128, 13824, 10530, 512, 2 * 10530
+
+    def lw(n, k):
+        return {"codes": (torch.randn(n, k, generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn),
+                "scale": torch.rand(n, generator=g) * 1e-4, "bias": (0.01 * torch.randn(n, generator=g)).bfloat16()}
+
+    layers, mods = {}, {}
+    for st in ("img", "txt"):
+        layers[st] = {"qkv": lw(3 * D, D), "proj": lw(D, D), "up": lw(Fh, D), "down": lw(D, Fh),
+                      "q_norm": (1 + 0.1 * torch.randn(Dh, generator=g)).bfloat16(),
+                      "k_norm": (1 + 0.1 * torch.randn(Dh, generator=g)).bfloat16()}
+        mods[st] = [(0.1 * torch.randn(D, generator=g)).bfloat16() for _ in range(6)]
+    img = torch.randn(Li, D, generator=g).bfloat16()
+    txt = torch.randn(Lt, D, generator=g).bfloat16()
+    ck = torch.randn(Lc, H, Dh, generator=g).bfloat16()
+    cv = torch.randn(Lc, H, Dh, generator=g).bfloat16()
+    ang = torch.rand(Li, Dh // 2, generator=g) * 6.283
+    cos, sin = ang.cos().bfloat16(), ang.sin().bfloat16()
+    t0 = time.perf_counter()
+    oi, ot = torch_eager.cfg4_block(img, txt, mods, layers, ck, cv, cos, sin, H)
+    dt = time.perf_counter() - t0
+    fl = 2 * (Li + Lt) * D * (3 * D + D + 2 * Fh) + 4 * (Li + Lt) * (Li + Lt + Lc) * D
+    return {"ms": round(dt * 1e3, 1), "TFLOP/s": round(fl / dt / 1e12, 3), "finite": bool(torch.isfinite(oi).all()),
+            "cfg5_chunk_ms_extrapolated": round(120 * dt * 1e3, 1),
+            "cfg5_fps_extrapolated": round(24 / (120 * dt), 4)}
 
 
 def run_reference(args):

@@ -182,6 +182,28 @@ int jo_attention_fwd(const void* q, const void* k, const void* v, void* out, int
                      int64_t heads, int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
                      const int64_t* v_strides, const int64_t* o_strides, float scale, int dtype, void* stream);
 
+/*
+ * Attention whose epilogue scatters its output to the ranks that own the
+ * query tokens (sequence parallelism, new entry; no reference counterpart:
+ * the reference runs attention on one GPU).  Computes jo_attention_fwd for
+ * batch 1 over this rank's `heads` heads of all Lq tokens in the gathered
+ * order, and stores query row r of head h into dst[k] at token r - seg_start[k],
+ * head head0 + h of a [tokens, all heads, 128] buffer with dst_token_stride
+ * elements between tokens, where seg_start[k] <= r < seg_start[k + 1]
+ * (seg_start has ranks + 1 entries, 0 first, Lq last).  This is the
+ * all-to-all that turns the head shard back into a token shard (replaces
+ * torch.distributed.all_to_all_single after attention).  Every segment must
+ * fit its destination's dst_tokens token rows and head0 + heads heads must
+ * fit the stride (JO_ERR_INVALID otherwise): a destination may be another
+ * GPU's memory (a peer pointer from jo_ipc_open).  1 <= ranks <= 8.  The
+ * caller synchronises the ranks before any rank reads its buffer.
+ */
+int jo_attention_fwd_scatter(const void* q, const void* k, const void* v, int64_t Lq, int64_t Lk, int64_t heads,
+                             int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, void* const* dst, const int64_t* seg_start, int ranks,
+                             int64_t head0, int64_t dst_token_stride, int64_t dst_tokens, float scale, int dtype,
+                             void* stream);
+
 /* Diagnostic: fault code left by an attention wait that timed out (0 = none);
  * reset != 0 clears it.  Synchronous; for tests and end-of-chunk checks. */
 int jo_attention_last_fault(int reset);

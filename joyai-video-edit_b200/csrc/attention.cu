@@ -207,12 +207,23 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t sv, int t, int 
            (acc || kk != 0) ? 1u : 0u);
 }
 
+constexpr int kMaxRanks = 8;  // destinations of the scattering epilogue
+
 struct Params {
   __nv_bfloat16* o;
   int64_t o_bs, o_ts, o_hs;  // output strides (elements)
   int Lq, Lk, H;
   int n_kt;                  // key tiles
   float scale_log2;          // softmax scale * log2(e)
+  // Scattering epilogue (nranks > 0, batch 1): query row r of the gathered
+  // order belongs to rank k with seg[k] <= r < seg[k + 1] and is stored at
+  // token r - seg[k], head head0 + h of that rank's [tokens, heads, 128]
+  // buffer dst[k] (dst_ts elements between tokens).
+  __nv_bfloat16* dst[kMaxRanks];
+  int seg[kMaxRanks + 1];
+  int nranks;
+  int head0;
+  int64_t dst_ts;
 };
 
 // barrier slots (8 bytes each) after the operand rings
@@ -433,6 +444,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = qb * 2 * BQ + t * BQ + quarter * 32 + lane;
       const float inv = 1.f / l;
       __nv_bfloat16* orow = p.o + (int64_t)b * p.o_bs + (int64_t)row * p.o_ts + (int64_t)h * p.o_hs;
+      if (p.nranks > 0) {
+        // owning rank of this query row (selects, no indexed parameter loads)
+        __nv_bfloat16* base = p.dst[0];
+        int s0 = 0;
+#pragma unroll
+        for (int i = 1; i < kMaxRanks; ++i)
+          if (i < p.nranks && row >= p.seg[i]) {
+            base = p.dst[i];
+            s0 = p.seg[i];
+          }
+        orow = base + (int64_t)(row - s0) * p.dst_ts + (int64_t)(p.head0 + h) * D;
+      }
 #pragma unroll 1
       for (int cch = 0; cch < 4; ++cch) {
         uint32_t o[32];
@@ -494,6 +517,93 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t B, int64_t L, i
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+struct ScatterSpec {
+  void* const* dst;
+  const int64_t* seg;
+  int ranks;
+  int64_t head0, dst_ts, dst_tokens;
+};
+
+static int launch(const char* what, const void* q, const void* k, const void* v, void* out, int64_t batch,
+                  int64_t Lq, int64_t Lk, int64_t heads, int64_t head_dim, const int64_t* q_strides,
+                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, float scale, int dtype,
+                  const ScatterSpec* sc, void* stream) {
+  JO_REQUIRE(dtype == JO_DTYPE_BF16, JO_ERR_DTYPE, "%s: only bf16 is supported", what);
+  JO_REQUIRE(head_dim == D, JO_ERR_INVALID, "%s: head_dim must be 128 (got %lld)", what, (long long)head_dim);
+  JO_REQUIRE(batch >= 0 && Lq >= 0 && Lk >= 0 && heads >= 0 && batch < 65536 && heads < 65536 && Lq < (1LL << 31) &&
+                 Lk < (1LL << 31),
+             JO_ERR_INVALID, "%s: invalid shape", what);
+  JO_REQUIRE(q_strides && k_strides && v_strides && o_strides, JO_ERR_INVALID, "%s: null strides", what);
+  if (batch == 0 || Lq == 0 || heads == 0) return JO_OK;
+  JO_REQUIRE(Lk > 0, JO_ERR_INVALID, "%s: attention over zero keys", what);
+  JO_REQUIRE(q && k && v && (out || sc), JO_ERR_INVALID, "%s: null tensor pointer", what);
+  const int64_t* S[4] = {q_strides, k_strides, v_strides, o_strides};
+  for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 3; ++j)
+      JO_REQUIRE(S[i][j] >= 0 && S[i][j] % 8 == 0, JO_ERR_ALIGN,
+                 "%s: batch / token / head strides must be non-negative multiples of 8 elements", what);
+  JO_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && (sc || aligned16(out)), JO_ERR_ALIGN,
+             "%s: tensors must be 16-byte aligned", what);
+  Params p;
+  p.o = static_cast<__nv_bfloat16*>(out);
+  p.o_bs = o_strides[0];
+  p.o_ts = o_strides[1];
+  p.o_hs = o_strides[2];
+  p.Lq = (int)Lq;
+  p.Lk = (int)Lk;
+  p.H = (int)heads;
+  p.n_kt = (int)((Lk + BK - 1) / BK);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.nranks = 0;
+  p.head0 = 0;
+  p.dst_ts = 0;
+  for (int i = 0; i < kMaxRanks; ++i) p.dst[i] = nullptr;
+  for (int i = 0; i <= kMaxRanks; ++i) p.seg[i] = (int)Lq;
+  if (sc) {
+    // Every store must land inside its destination: a destination may be
+    // another GPU's memory.
+    JO_REQUIRE(batch == 1, JO_ERR_INVALID, "%s: the scattering form takes one batch", what);
+    JO_REQUIRE(sc->ranks >= 1 && sc->ranks <= kMaxRanks && sc->dst && sc->seg, JO_ERR_INVALID,
+               "%s: 1..%d destinations with their segment table required", what, kMaxRanks);
+    JO_REQUIRE(sc->head0 >= 0 && sc->dst_ts % 8 == 0 && sc->dst_ts >= (sc->head0 + heads) * D, JO_ERR_INVALID,
+               "%s: destination token stride %lld too small for heads %lld..%lld of 128", what,
+               (long long)sc->dst_ts, (long long)sc->head0, (long long)(sc->head0 + heads));
+    JO_REQUIRE(sc->seg[0] == 0 && sc->seg[sc->ranks] == Lq, JO_ERR_INVALID,
+               "%s: the segments must cover the %lld query rows", what, (long long)Lq);
+    for (int r = 0; r < sc->ranks; ++r) {
+      JO_REQUIRE(sc->seg[r + 1] >= sc->seg[r] && sc->seg[r + 1] - sc->seg[r] <= sc->dst_tokens, JO_ERR_INVALID,
+                 "%s: segment %d (%lld rows) is negative or exceeds the destination's %lld token rows", what, r,
+                 (long long)(sc->seg[r + 1] - sc->seg[r]), (long long)sc->dst_tokens);
+      JO_REQUIRE(sc->dst[r] && aligned16(sc->dst[r]), JO_ERR_ALIGN,
+                 "%s: destination %d is null or not 16-byte aligned", what, r);
+      p.dst[r] = static_cast<__nv_bfloat16*>(sc->dst[r]);
+      p.seg[r] = (int)sc->seg[r];
+    }
+    p.seg[sc->ranks] = (int)Lq;
+    p.nranks = sc->ranks;
+    p.head0 = (int)sc->head0;
+    p.dst_ts = sc->dst_ts;
+  }
+  int st = require_sm100();
+  if (st != JO_OK) return st;
+  CUtensorMap tq, tk, tv;
+  if (!make_map(&tq, q, batch, Lq, heads, q_strides[0], q_strides[1], q_strides[2]) ||
+      !make_map(&tk, k, batch, Lk, heads, k_strides[0], k_strides[1], k_strides[2]) ||
+      !make_map(&tv, v, batch, Lk, heads, v_strides[0], v_strides[1], v_strides[2])) {
+    set_error("%s: cuTensorMapEncodeTiled failed", what);
+    return JO_ERR_CUDA;
+  }
+  static bool attr[kMaxDevices] = {};
+  const int dev = device_slot();
+  if (!attr[dev]) {
+    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr[dev] = true;
+  }
+  dim3 grid((unsigned)((Lq + 2 * BQ - 1) / (2 * BQ)), (unsigned)heads, (unsigned)batch);
+  attn_fwd_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  return check_launch(what);
+}
+
 }  // namespace attn
 }  // namespace jo
 
@@ -502,53 +612,19 @@ extern "C" {
 int jo_attention_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t Lq, int64_t Lk,
                      int64_t heads, int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
                      const int64_t* v_strides, const int64_t* o_strides, float scale, int dtype, void* stream) {
-  using namespace jo;
-  const char* what = "attention_fwd";
-  JO_REQUIRE(dtype == JO_DTYPE_BF16, JO_ERR_DTYPE, "%s: only bf16 is supported", what);
-  JO_REQUIRE(head_dim == attn::D, JO_ERR_INVALID, "%s: head_dim must be 128 (got %lld)", what, (long long)head_dim);
-  JO_REQUIRE(batch >= 0 && Lq >= 0 && Lk >= 0 && heads >= 0 && batch < 65536 && heads < 65536 && Lq < (1LL << 31) &&
-                 Lk < (1LL << 31),
-             JO_ERR_INVALID, "%s: invalid shape", what);
-  JO_REQUIRE(q_strides && k_strides && v_strides && o_strides, JO_ERR_INVALID, "%s: null strides", what);
-  if (batch == 0 || Lq == 0 || heads == 0) return JO_OK;
-  JO_REQUIRE(Lk > 0, JO_ERR_INVALID, "%s: attention over zero keys", what);
-  JO_REQUIRE(q && k && v && out, JO_ERR_INVALID, "%s: null tensor pointer", what);
-  const int64_t* S[4] = {q_strides, k_strides, v_strides, o_strides};
-  for (int i = 0; i < 4; ++i)
-    for (int j = 0; j < 3; ++j)
-      JO_REQUIRE(S[i][j] >= 0 && S[i][j] % 8 == 0, JO_ERR_ALIGN,
-                 "%s: batch / token / head strides must be non-negative multiples of 8 elements", what);
-  JO_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out), JO_ERR_ALIGN,
-             "%s: tensors must be 16-byte aligned", what);
-  int st = require_sm100();
-  if (st != JO_OK) return st;
-  CUtensorMap tq, tk, tv;
-  if (!attn::make_map(&tq, q, batch, Lq, heads, q_strides[0], q_strides[1], q_strides[2]) ||
-      !attn::make_map(&tk, k, batch, Lk, heads, k_strides[0], k_strides[1], k_strides[2]) ||
-      !attn::make_map(&tv, v, batch, Lk, heads, v_strides[0], v_strides[1], v_strides[2])) {
-    set_error("%s: cuTensorMapEncodeTiled failed", what);
-    return JO_ERR_CUDA;
-  }
-  attn::Params p;
-  p.o = static_cast<__nv_bfloat16*>(out);
-  p.o_bs = o_strides[0];
-  p.o_ts = o_strides[1];
-  p.o_hs = o_strides[2];
-  p.Lq = (int)Lq;
-  p.Lk = (int)Lk;
-  p.H = (int)heads;
-  p.n_kt = (int)((Lk + attn::BK - 1) / attn::BK);
-  p.scale_log2 = scale * 1.4426950408889634f;
-  static bool attr[kMaxDevices] = {};
-  const int dev = device_slot();
-  if (!attr[dev]) {
-    cudaFuncSetAttribute(attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES);
-    attr[dev] = true;
-  }
-  dim3 grid((unsigned)((Lq + 2 * attn::BQ - 1) / (2 * attn::BQ)), (unsigned)heads, (unsigned)batch);
-  attn::attn_fwd_kernel<<<grid, attn::THREADS, attn::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv,
-                                                                                                      p);
-  return check_launch(what);
+  return jo::attn::launch("attention_fwd", q, k, v, out, batch, Lq, Lk, heads, head_dim, q_strides, k_strides,
+                          v_strides, o_strides, scale, dtype, nullptr, stream);
+}
+
+int jo_attention_fwd_scatter(const void* q, const void* k, const void* v, int64_t Lq, int64_t Lk, int64_t heads,
+                             int64_t head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, void* const* dst, const int64_t* seg_start, int ranks,
+                             int64_t head0, int64_t dst_token_stride, int64_t dst_tokens, float scale, int dtype,
+                             void* stream) {
+  const int64_t zero[3] = {0, 0, 0};
+  const jo::attn::ScatterSpec sc{dst, seg_start, ranks, head0, dst_token_stride, dst_tokens};
+  return jo::attn::launch("attention_fwd_scatter", q, k, v, nullptr, 1, Lq, Lk, heads, head_dim, q_strides,
+                          k_strides, v_strides, zero, scale, dtype, &sc, stream);
 }
 
 // Fault code of the attention kernel's bounded waits (0 = none); reset != 0

@@ -13,6 +13,7 @@ Extra entry points with no reference counterpart:
   * ``norm_modulate_quant_fp8`` — norm -> adaLN modulate -> per-token FP8 in one pass;
   * ``fp8_scaled_mm_gelu``      — FP8 GEMM with the GELU-tanh epilogue fused;
   * ``attention``               — tcgen05 attention forward over NHD bf16 tensors
+  * ``attention_scatter``       — the same, output rows stored to the ranks owning them
     (the reference model's external FA4 / SDPA call, dit.py:150-178);
   * broadcast modulation in ``fused_norm_scale_shift``: scale/shift given as an
     expanded view (row stride 0) are read in place instead of being materialised.
@@ -40,6 +41,7 @@ __all__ = [
     "qk_norm_rope_strided",
     "fp8_scaled_mm_residual",
     "attention",
+    "attention_scatter",
     "rope_apply",
 ]
 
@@ -486,6 +488,43 @@ def attention(query, key, value, *, out=None, scale: Optional[float] = None):
     if out is not None:
         return out
     return o[0] if squeeze else o
+
+
+
+def attention_scatter(query, key, value, dst_ptrs, seg_start, head0, total_heads, dst_tokens, *,
+                      scale: Optional[float] = None):
+    """attention() over this rank's heads of all tokens (q [Lq, h, 128], k and v
+    [Lk, h, 128], bf16, batch 1) whose output rows go straight to the ranks that
+    own them: query row r with seg_start[k] <= r < seg_start[k + 1] is stored at
+    token r - seg_start[k], head head0 + j of the [dst_tokens, total_heads, 128]
+    bf16 buffer at device address dst_ptrs[k] (a peer rank's buffer through
+    joyomni_stack.peer).  The sequence-parallel all-to-all after attention,
+    fused into the attention epilogue (new entry); the caller synchronises the
+    ranks before they read their buffers."""
+    q, k, v = query, key, value
+    for name, t in (("query", q), ("key", k), ("value", v)):
+        _chk(t.is_cuda, f"{name} must be a CUDA tensor")
+        _chk(t.dim() == 3, f"{name} must be [L, H, D]")
+        _chk(t.dtype == torch.bfloat16, f"{name} must be BFloat16")
+        _chk(t.size(2) == 128 and t.stride(2) == 1, f"{name} must have a contiguous head_dim of 128")
+    Lq, H, Dh = q.shape
+    _chk(k.shape[1] == H and v.shape[1] == H and k.shape[0] == v.shape[0], "key / value shapes do not match")
+    R = len(dst_ptrs)
+    _chk(1 <= R <= 8 and len(seg_start) == R + 1, "1..8 destinations and ranks + 1 segment starts required")
+    _chk(seg_start[0] == 0 and seg_start[R] == Lq, "the segments must cover the query rows")
+    _chk(all(0 <= seg_start[i + 1] - seg_start[i] <= dst_tokens for i in range(R)),
+         "every segment must fit the destinations' dst_tokens rows")
+    _chk(0 <= head0 and head0 + H <= total_heads, "heads head0 .. head0 + H must fit total_heads")
+    sc = (1.0 / math.sqrt(Dh)) if scale is None else float(scale)
+
+    def strides(t):
+        return (ctypes.c_int64 * 3)(0, t.stride(0), t.stride(1))
+    arr = (ctypes.c_void_p * R)(*[int(p) for p in dst_ptrs])
+    seg = (ctypes.c_int64 * (R + 1))(*[int(s) for s in seg_start])
+    with _Device(q) as st:
+        _check(_L.jo_attention_fwd_scatter(q.data_ptr(), k.data_ptr(), v.data_ptr(), Lq, k.shape[0], H, Dh,
+                                           strides(q), strides(k), strides(v), arr, seg, R, head0,
+                                           total_heads * Dh, dst_tokens, sc, _lib.JO_DTYPE_BF16, st))
 
 
 from . import _torch_ops  # noqa: E402,F401  (registers torch.ops.joyomni_ops.*)

@@ -58,6 +58,9 @@ SIGNATURES = {
     "jo_rope_apply": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "jo_attention_fwd": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
                          ctypes.POINTER(_i64), ctypes.POINTER(_i64), _f32, _i32, _p],
+    "jo_attention_fwd_scatter": [_p, _p, _p, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                                 ctypes.POINTER(_i64), _p, ctypes.POINTER(_i64), _i32, _i64, _i64, _i64, _f32, _i32,
+                                 _p],
     "jo_attention_last_fault": [_i32],
     "jo_gemm_last_fault": [_i32],
     "jo_fp8_scaled_mm_scatter": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _p, _i32, _i32, _i32, _i32, _i64, _i64,

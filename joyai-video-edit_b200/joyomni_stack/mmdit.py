@@ -250,14 +250,19 @@ class LayerKV:
 class PeerExchange:
     """Per-layer view of the peer exchange: the head-sharded q buffer, the
     gathered-order segments (offset, image rows, text rows, first image token)
-    of every rank, the full RoPE tables, and the 3 x P destination addresses
-    (q, k, v of every rank) handed to the scattering QKV projection."""
+    of every rank, the full RoPE tables, the 3 x P destination addresses
+    (q, k, v of every rank) handed to the scattering QKV projection, and the
+    attention output buffers of every rank that the scattering attention
+    epilogue writes."""
     region: object
     q: torch.Tensor
     seg: list
     cos: torch.Tensor
     sin: torch.Tensor
     dst: list
+    o: Optional[torch.Tensor] = None     # this rank's [tokens, heads, Dh] attention output (all heads)
+    odst: Optional[list] = None          # every rank's attention output buffer (device addresses)
+    oseg: Optional[list] = None          # rank segment starts of the gathered order (P + 1)
 
 
 class Block:
@@ -347,16 +352,30 @@ class Block:
             kv.last_q = q.clone()
         self._mark("qk_norm_rope")
         k_all, v_all = kv.keys()
-        o = attend(q, k_all, v_all, self.cfg.attention)
-        self._mark("attention")
-        # Every layer shares the one head-sharded q buffer in the peer region:
-        # a faster rank's next-layer scatter may only start once this rank's
-        # attention has finished reading q.  heads_to_seq is an NCCL all-to-all
-        # that no rank leaves before every rank has entered it (after its
-        # attention), which gives that ordering; an asynchronous or peer-based
-        # output exchange would need an explicit region.sync() here instead.
-        o = sp.heads_to_seq(o).reshape(Li + txt.shape[0], D)
-        self._mark("output_all_to_all")
+        L = Li + txt.shape[0]
+        if self.cfg.attention == "joyomni" and ex.o is not None:
+            # The attention epilogue stores every output row into the owning
+            # rank's buffer (peer memory for P > 1): the output all-to-all.
+            jo.attention_scatter(q, k_all, v_all, ex.odst, ex.oseg, sp.rank * sp.local_heads, cfg.heads,
+                                 ex.o.shape[0])
+            self._mark("attention")
+            # One sync orders both hazards of the shared buffers: every rank's
+            # rows have landed before this rank's projection reads its buffer,
+            # and no rank's next-layer QKV scatter overwrites the q buffer (or
+            # next attention the output buffer) that a slower rank still reads.
+            if ex.region is not None:
+                ex.region.sync()
+            o = ex.o[:L].reshape(L, D)
+        else:
+            o = attend(q, k_all, v_all, self.cfg.attention)
+            self._mark("attention")
+            # Every layer shares the one head-sharded q buffer in the peer region:
+            # a faster rank's next-layer scatter may only start once this rank's
+            # attention has finished reading q.  heads_to_seq is an NCCL all-to-all
+            # that no rank leaves before every rank has entered it (after its
+            # attention), which gives that ordering.
+            o = sp.heads_to_seq(o).reshape(L, D)
+        self._mark("output_exchange")
         img = self._tail(self.img, im, img, o[:Li])
         txt = self._tail(self.txt, tm, txt, o[Li:])
         self._mark("proj_ffn_gemms")
@@ -448,6 +467,10 @@ class Stack:
         rows = sp.total_len + cfg.cache_chunks * cfg.img_tokens
         lay = RegionLayout()
         lay.add("q", (sp.total_len, hpr, Dh))
+        # attention output of this rank's tokens, all heads (identical size on
+        # every rank: the largest shard)
+        ocap = max(sp.shard_len(r) for r in range(sp.world))
+        lay.add("o", (ocap, cfg.heads, Dh))
         for i in range(n):
             lay.add(f"k{i}", (rows, hpr, Dh))
             lay.add(f"v{i}", (rows, hpr, Dh))
@@ -460,12 +483,17 @@ class Stack:
             seg.append((off, isz[r], tsz[r], shard_range(cfg.img_tokens, sp.world, r)[0]))
             off += isz[r] + tsz[r]
         q = self.region.tensor("q")
+        # JOYOMNI_ATTN_SCATTER=0 keeps the NCCL all-to-all after attention (comparison)
+        scatter_out = os.environ.get("JOYOMNI_ATTN_SCATTER", "1") != "0"
+        o = self.region.tensor("o") if scatter_out else None
+        odst = [self.region.ptr(r, "o") for r in range(sp.world)] if scatter_out else None
+        oseg = [s[0] for s in seg] + [sp.total_len]
         kvs = []
         for i in range(n):
             kv = LayerKV(cfg, sp, device, k=self.region.tensor(f"k{i}"), v=self.region.tensor(f"v{i}"))
             kv.peer = PeerExchange(self.region if sp.world > 1 else None, q, seg, cos, sin,
                                    [self.region.ptr(r, name) for name in ("q", f"k{i}", f"v{i}")
-                                    for r in range(sp.world)])
+                                    for r in range(sp.world)], o, odst, oseg)
             kvs.append(kv)
         return kvs
 

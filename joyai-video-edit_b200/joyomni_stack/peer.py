@@ -1,17 +1,22 @@
 """Peer-memory exchange region for Ulysses sequence parallelism on one node.
 
 Every rank allocates one region with the same layout (the head-sharded q
-buffer and every layer's [current | cache] K/V buffers), exports its CUDA IPC
-handle and opens the others' (legacy CUDA IPC through the C ABI: plain
-peer-to-peer mappings, no NVLink multicast objects).  The QKV projection's
-epilogue (jo_fp8_scaled_mm_scatter) then stores each (token, head) straight
-into the owning rank's region over NVLink, which replaces the all-to-all that
-turns the token shard into a head shard.
+buffer, the attention output buffer of its tokens and every layer's
+[current | cache] K/V buffers), exports its CUDA IPC handle and opens the
+others' (legacy CUDA IPC through the C ABI: plain peer-to-peer mappings, no
+NVLink multicast objects).  The QKV projection's epilogue
+(jo_fp8_scaled_mm_scatter) then stores each (token, head) straight into the
+owning rank's region over NVLink, which replaces the all-to-all that turns the
+token shard into a head shard; the attention epilogue
+(jo_attention_fwd_scatter) stores each output row back into the region of the
+rank that owns the token, which replaces the all-to-all after attention.
 
 Ordering: a rank reads its region only after a one-element NCCL all-reduce
-that every rank enqueues after its scatters (sync()); the same call after the
-KV-cache commit keeps the next chunk's scatters from overtaking the commit
-copies of a slower rank.
+that every rank enqueues after its scatters (sync()), once after the QKV
+projections and once after attention; the second also keeps a faster rank's
+next-layer scatters from overwriting the q buffer a slower rank's attention
+still reads.  The same call after the KV-cache commit keeps the next chunk's
+scatters from overtaking the commit copies of a slower rank.
 """
 from __future__ import annotations
 

@@ -64,6 +64,21 @@ def test_invalid_arguments_rejected_before_any_launch():
     assert L.jo_fp8_scaled_mm_scatter(16, 16, 16, 16, None, 8, 96, 64, _lib.JO_DTYPE_BF16, dst, 3, 1, 1, 32,
                                       4, 10, None) == _lib.JO_ERR_INVALID
     assert "do not fit" in _lib.last_error()
+    # attention output scattered to owning ranks: a segment longer than the
+    # destination's token rows, or heads beyond its stride, is refused
+    st3 = (ctypes.c_int64 * 3)(0, 256, 128)
+    adst = (ctypes.c_void_p * 2)(256, 512)
+    seg = (ctypes.c_int64 * 3)(0, 70, 100)
+    assert L.jo_attention_fwd_scatter(256, 256, 256, 100, 50, 2, 128, st3, st3, st3, adst, seg, 2, 0, 4 * 128,
+                                      64, 0.1, _lib.JO_DTYPE_BF16, None) == _lib.JO_ERR_INVALID
+    assert "exceeds the destination" in _lib.last_error()
+    assert L.jo_attention_fwd_scatter(256, 256, 256, 100, 50, 2, 128, st3, st3, st3, adst, seg, 2, 3, 4 * 128,
+                                      128, 0.1, _lib.JO_DTYPE_BF16, None) == _lib.JO_ERR_INVALID
+    assert "too small" in _lib.last_error()
+    bad = (ctypes.c_int64 * 3)(0, 70, 99)
+    assert L.jo_attention_fwd_scatter(256, 256, 256, 100, 50, 2, 128, st3, st3, st3, adst, bad, 2, 0, 4 * 128,
+                                      128, 0.1, _lib.JO_DTYPE_BF16, None) == _lib.JO_ERR_INVALID
+    assert "cover" in _lib.last_error()
 
 
 def test_status_mapping():

@@ -116,3 +116,30 @@ def test_attention_config4_shape(jo, cuda):
         e, e_sdpa = check(out[rows, h:h + 1][None], qs, ks, vs)
         print(f"head {h}: rel RMS vs fp32 {e:.2e} (torch bf16 SDPA {e_sdpa:.2e})")
     jo.check_gemm_fault(cuda)
+
+
+def test_attention_scatter_emulated_ranks(jo, cuda):
+    """The scattering epilogue (jo_attention_fwd_scatter) on one GPU with three
+    emulated ranks: every query row lands, bit-identical to attention(), at its
+    owner's token row and at heads head0 .. head0 + h of the owner's
+    [tokens, all heads, 128] buffer; nothing else in the buffers changes."""
+    g = torch.Generator(device=cuda).manual_seed(21)
+    Lq, Lk, h, total, head0 = 700, 1500, 2, 6, 2
+    segs = [0, 250, 450, 700]
+    cap = 260
+    q = torch.randn(Lq, h, 128, generator=g, device=cuda).to(torch.bfloat16)
+    k = torch.randn(Lk, h, 128, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(Lk, h, 128, generator=g, device=cuda).to(torch.bfloat16)
+    ref = jo.attention(q, k, v)
+    dst = [torch.full((cap, total, 128), -7.0, dtype=torch.bfloat16, device=cuda) for _ in range(3)]
+    for rep in range(2):
+        jo.attention_scatter(q, k, v, [d.data_ptr() for d in dst], segs, head0, total, cap)
+        torch.cuda.synchronize()
+        for r in range(3):
+            n = segs[r + 1] - segs[r]
+            assert torch.equal(dst[r][:n, head0:head0 + h], ref[segs[r]:segs[r + 1]])
+            assert bool((dst[r][:n, :head0] == -7.0).all()) and bool((dst[r][:n, head0 + h:] == -7.0).all())
+            assert bool((dst[r][n:] == -7.0).all())
+    with pytest.raises(RuntimeError):
+        jo.attention_scatter(q, k, v, [d.data_ptr() for d in dst], segs, head0, total, 249)
+    jo.check_gemm_fault(cuda)

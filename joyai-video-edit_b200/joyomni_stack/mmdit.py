@@ -487,7 +487,8 @@ class Stack:
         scatter_out = os.environ.get("JOYOMNI_ATTN_SCATTER", "1") != "0"
         o = self.region.tensor("o") if scatter_out else None
         odst = [self.region.ptr(r, "o") for r in range(sp.world)] if scatter_out else None
-        oseg = [s[0] for s in seg] + [sp.total_len]
+        oseg = sp.gathered_segment_starts()
+        assert oseg[:-1] == [s[0] for s in seg]
         kvs = []
         for i in range(n):
             kv = LayerKV(cfg, sp, device, k=self.region.tensor(f"k{i}"), v=self.region.tensor(f"v{i}"))

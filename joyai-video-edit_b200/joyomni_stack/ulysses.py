@@ -93,6 +93,16 @@ class SeqParallel:
             off += self.shard_len(r)
         return segs
 
+    def gathered_segment_starts(self):
+        """First row of every rank's tokens in the gathered order, then the
+        total: rank k owns rows starts[k] .. starts[k + 1] (the segment table of
+        the attention epilogue that stores each output row on its owner)."""
+        starts, off = [], 0
+        for r in range(self.world):
+            starts.append(off)
+            off += self.shard_len(r)
+        return starts + [off]
+
     # -- exchanges -------------------------------------------------------------
     def seq_to_heads(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """[L_local, H, Dh] (this rank's tokens, all heads) -> [L_total, H/P, Dh]

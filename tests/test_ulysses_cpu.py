@@ -1,6 +1,8 @@
 """Ulysses exchange logic on CPU with gloo, world size 2 (and 3 for uneven
-shards): sequence->head->sequence round trip, and attention computed head-
-sharded equals attention on the full sequence."""
+shards): sequence->head->sequence round trip, attention computed head-
+sharded equals attention on the full sequence, and the segment table of the
+scattering attention epilogue rebuilds each rank's rows exactly as the
+head->sequence all-to-all does."""
 import os
 import socket
 
@@ -46,7 +48,22 @@ def _worker(rank, world, port, img, txt, heads, q):
                                                                full[2].permute(1, 0, 2)[None])[0].permute(1, 0, 2)
         ref_local = torch.cat((ref[a:b], ref[img + c: img + d]), 0)
         err = (o - ref_local).abs().max().item()
-        q.put((rank, ok_rt, err, sp.local_len))
+        # the attention epilogue's scatter rule (jo_attention_fwd_scatter with
+        # the segment table gathered_segment_starts): row i of rank r's
+        # head-sharded output goes to the owner k of row i at token
+        # i - starts[k], heads r * H/P .. -- emulated here with every rank's
+        # head-sharded output, it must rebuild exactly what heads_to_seq gives
+        hs = qh.contiguous()
+        every = [torch.empty_like(hs) for _ in range(world)]
+        dist.all_gather(every, hs)
+        starts = sp.gathered_segment_starts()
+        mine = torch.full((sp.local_len, heads, Dh), float("nan"))
+        hpr = heads // world
+        for r in range(world):
+            for i in range(starts[rank], starts[rank + 1]):
+                mine[i - starts[rank], r * hpr:(r + 1) * hpr] = every[r][i]
+        ok_sc = starts[-1] == sp.total_len and torch.equal(mine, sp.heads_to_seq(hs))
+        q.put((rank, ok_rt and ok_sc, err, sp.local_len))
     finally:
         dist.destroy_process_group()
 
